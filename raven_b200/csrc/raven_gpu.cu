@@ -1,0 +1,916 @@
+// C-ABI implementation of the B200 query engine (include/raven_gpu.h).
+//
+// Device data layout (HBM):
+//   vectors   n x dim f32 (row-major, as given)
+//   adj       n x r_pad u32, r_pad = roundup(r_max, 32): the HybridBlockedCsr
+//             main block, SENTINEL padded; one 128 B line per 32 neighbours
+//   sq4/sq8   n x stride u8 codes, stride = pow2 >= 16 bytes (64 B for dim 128
+//             SQ4, 128 B for dim 128 SQ8), zero padded past the real code
+//   nav       slot[n] -> nav_off[slot..slot+1] into nav_edges (global ids)
+//   adaptive  sorted sample distances (<= 2000) + per-call rank->ef table
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/raven_gpu.h"
+#include "host_index.h"
+#include "search_kernel.cuh"
+
+using namespace raven_dev;
+
+struct raven_graph {
+  raven::HostGraph g;
+};
+
+struct raven_index {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  uint64_t n = 0;
+  uint32_t dim = 0, dim_pad = 0, r_max = 0, r_pad = 0, entry = 0;
+  float* d_vec = nullptr;
+  uint32_t* d_adj = nullptr;
+  bool has_q[2] = {false, false};
+  uint32_t q_stride[2] = {0, 0};
+  uint8_t* d_codes[2] = {nullptr, nullptr};
+  float* d_qparams[2] = {nullptr, nullptr};  // 5*dim
+  std::vector<float> h_qparams[2];
+  bool has_nav = false;
+  uint32_t nav_entry = 0, nav_max_level = 0, nav_k = 0;
+  uint32_t* d_nav_slot = nullptr;
+  uint32_t* d_nav_off = nullptr;
+  uint32_t* d_nav_edges = nullptr;
+  std::vector<float> h_samples;
+  float* d_samples = nullptr;
+  // launch tuning
+  int hash_bits_override = 0;
+  int spill_bits = 14;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CU(call)                                                                        \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess) return fail(RAVEN_ECUDA, std::string(#call ": ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+uint32_t next_pow2(uint32_t x) {
+  uint32_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// Quantisation on the device: SQ4Params::encode_all (src/quant/sq4.rs:108-125)
+// and SQ8Params::encode_all (src/quant/sq8.rs:100-111). One thread per output
+// 4-byte word; padding bytes are zero.
+// ---------------------------------------------------------------------------
+__global__ void encode_kernel(const float* __restrict__ v, uint64_t n, uint32_t dim, const float* __restrict__ inv,
+                              const float* __restrict__ neg, float levels, int sq4, uint32_t stride,
+                              uint32_t* __restrict__ out) {
+  const uint32_t words = stride / 4;
+  const uint64_t total = n * words;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t row = t / words;
+    const uint32_t w = (uint32_t)(t % words);
+    const float* r = v + row * dim;
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t byte = w * 4 + b;
+      uint32_t val = 0;
+      if (sq4) {
+        const uint32_t d0 = 2 * byte, d1 = 2 * byte + 1;
+        uint32_t lo = d0 < dim ? quantize(r[d0], inv[d0], neg[d0], levels) : 0u;
+        uint32_t hi = d1 < dim ? quantize(r[d1], inv[d1], neg[d1], levels) : 0u;
+        val = lo | (hi << 4);
+      } else {
+        val = byte < dim ? quantize(r[byte], inv[byte], neg[byte], levels) : 0u;
+      }
+      word |= (val & 0xFFu) << (8 * b);
+    }
+    out[t] = word;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Exact kNN (recall ground truth). Block: 64 queries x 64-row tiles of the
+// base, 256 threads, 4x4 register micro-tile of squared distances
+// (sum of fma(d,d) over dims: exact for integer-valued data), then a per-query
+// sorted top-k (k <= 32) kept in shared memory, ties by id. The base range is
+// split over gridDim.y; a second kernel merges the splits.
+// ---------------------------------------------------------------------------
+constexpr int KQ = 64, KB = 64, KD = 16, KMAXK = 32;
+
+__global__ void __launch_bounds__(256) knn_tile_kernel(const float* __restrict__ base, uint64_t n,
+                                                        const float* __restrict__ q, uint64_t nq, uint32_t dim,
+                                                        uint32_t k, uint64_t split_rows, uint32_t* __restrict__ out_i,
+                                                        float* __restrict__ out_d) {
+  __shared__ float qs[KD][KQ + 1];
+  __shared__ float bs[KD][KB + 1];
+  __shared__ float dt[KQ][KB + 1];
+  __shared__ float tk_d[KQ][KMAXK];
+  __shared__ uint32_t tk_i[KQ][KMAXK];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const uint64_t q0 = (uint64_t)blockIdx.x * KQ;
+  const uint64_t r_begin = (uint64_t)blockIdx.y * split_rows;
+  const uint64_t r_end = min(n, r_begin + split_rows);
+  for (int i = tid; i < KQ * KMAXK; i += 256) {
+    tk_d[i / KMAXK][i % KMAXK] = __int_as_float(0x7f800000);
+    tk_i[i / KMAXK][i % KMAXK] = 0xffffffffu;
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  for (uint64_t b0 = r_begin; b0 < r_end; b0 += KB) {
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (uint32_t d0 = 0; d0 < dim; d0 += KD) {
+      for (int i = tid; i < KD * KQ; i += 256) {
+        int qq = i / KD, dd = i % KD;
+        uint64_t qi = q0 + qq;
+        qs[dd][qq] = (qi < nq && d0 + dd < dim) ? q[qi * dim + d0 + dd] : 0.0f;
+      }
+      for (int i = tid; i < KD * KB; i += 256) {
+        int bb = i / KD, dd = i % KD;
+        uint64_t bi = b0 + bb;
+        bs[dd][bb] = (bi < r_end && d0 + dd < dim) ? base[bi * dim + d0 + dd] : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll 8
+      for (int dd = 0; dd < KD; ++dd) {
+        float a[4], b[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = qs[dd][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = bs[dd][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float t = a[i] - b[j];
+            acc[i][j] = fmaf(t, t, acc[i][j]);
+          }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dt[ty * 4 + i][tx * 4 + j] = acc[i][j];
+    __syncthreads();
+    // top-k update: warp w owns queries w, w+8, ...
+    for (int qq = warp; qq < KQ; qq += 8) {
+      const float thr = tk_d[qq][k - 1];
+      const uint32_t thr_i = tk_i[qq][k - 1];
+      for (int c = lane; c < KB; c += 32) {
+        uint64_t bi = b0 + c;
+        float d = dt[qq][c];
+        bool cand = bi < r_end && (d < thr || (d == thr && (uint32_t)bi < thr_i));
+        uint32_t m = __ballot_sync(0xffffffffu, cand);
+        while (m) {
+          int src = __ffs(m) - 1;
+          m &= m - 1;
+          float cd = __shfl_sync(0xffffffffu, d, src);
+          uint32_t ci = (uint32_t)(b0 + c - lane + src);
+          // insert (cd, ci) into the sorted list (lane 0 does it)
+          if (lane == 0) {
+            int pos = (int)k;
+            while (pos > 0 && (tk_d[qq][pos - 1] > cd || (tk_d[qq][pos - 1] == cd && tk_i[qq][pos - 1] > ci))) --pos;
+            if (pos < (int)k) {
+              for (int t = (int)k - 1; t > pos; --t) {
+                tk_d[qq][t] = tk_d[qq][t - 1];
+                tk_i[qq][t] = tk_i[qq][t - 1];
+              }
+              tk_d[qq][pos] = cd;
+              tk_i[qq][pos] = ci;
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int i = tid; i < KQ * (int)k; i += 256) {
+    int qq = i / k, j = i % k;
+    uint64_t qi = q0 + qq;
+    if (qi < nq) {
+      size_t o = ((size_t)blockIdx.y * nq + qi) * k + j;
+      out_i[o] = tk_i[qq][j];
+      out_d[o] = tk_d[qq][j];
+    }
+  }
+}
+
+// Merge sorted top-k lists: per query, `lists` lists of k (dist, id) entries,
+// ascending (dist, id) -> k. One warp per query, rank counting.
+__global__ void knn_merge_kernel(const uint32_t* __restrict__ in_i, const float* __restrict__ in_d, uint32_t lists,
+                                 uint64_t nq, uint32_t k, uint32_t* __restrict__ out_i, float* __restrict__ out_d) {
+  const uint64_t qi = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (qi >= nq) return;
+  const uint32_t total = lists * k;
+  for (uint32_t e = lane; e < total; e += 32) {
+    const uint32_t l = e / k, j = e % k;
+    const size_t o = ((size_t)l * nq + qi) * k + j;
+    const float d = in_d[o];
+    const uint32_t id = in_i[o];
+    uint32_t rank = 0;
+    for (uint32_t f = 0; f < total; ++f) {
+      const size_t p = ((size_t)(f / k) * nq + qi) * k + f % k;
+      const float df = in_d[p];
+      const uint32_t idf = in_i[p];
+      rank += (df < d) || (df == d && (idf < id || (idf == id && f < e)));
+    }
+    if (rank < k) {
+      out_i[qi * k + rank] = id;
+      out_d[qi * k + rank] = d;
+    }
+  }
+}
+
+// Shard merge: ids are shard-local; global id = shard * shard_size + local.
+__global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ ds,
+                                   const uint32_t* __restrict__ counts, uint32_t n_shards, uint64_t nq, uint32_t k,
+                                   uint64_t shard_size, uint32_t* __restrict__ out_i, float* __restrict__ out_d,
+                                   uint32_t* __restrict__ out_c) {
+  const uint64_t qi = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (qi >= nq) return;
+  const uint32_t total = n_shards * k;
+  uint32_t valid_total = 0;
+  for (uint32_t sh = 0; sh < n_shards; ++sh) valid_total += counts ? min(counts[sh * nq + qi], k) : k;
+  for (uint32_t e = lane; e < total; e += 32) {
+    const uint32_t sh = e / k, r = e % k;
+    const uint32_t cnt = counts ? min(counts[sh * nq + qi], k) : k;
+    if (r >= cnt) continue;
+    const size_t o = ((size_t)sh * nq + qi) * k + r;
+    const float d = ds[o];
+    uint32_t rank = 0;
+    for (uint32_t f = 0; f < total; ++f) {
+      const uint32_t fs = f / k, fr = f % k;
+      const uint32_t fc = counts ? min(counts[fs * nq + qi], k) : k;
+      if (fr >= fc) continue;
+      const float df = ds[((size_t)fs * nq + qi) * k + fr];
+      rank += (df < d) || (df == d && (fs < sh || (fs == sh && fr < r)));
+    }
+    if (rank < k) {
+      out_i[qi * k + rank] = (uint32_t)(sh * shard_size + ids[o]);
+      out_d[qi * k + rank] = d;
+    }
+  }
+  const uint32_t outc = min(valid_total, k);
+  for (uint32_t r = outc + lane; r < k; r += 32) {
+    out_i[qi * k + r] = 0;
+    out_d[qi * k + r] = 0.0f;
+  }
+  if (lane == 0 && out_c) out_c[qi] = outc;
+}
+
+// ---------------------------------------------------------------------------
+// Search launch.
+// ---------------------------------------------------------------------------
+template <int QUANT, int CPL, int PT>
+cudaError_t launch_t(const SearchArgs& a, uint32_t smem_per_block, int grid, cudaStream_t st) {
+  auto k = search_kernel<QUANT, CPL, PT>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
+  if (e != cudaSuccess) return e;
+  k<<<grid, kWarpsPerBlock * 32, smem_per_block, st>>>(a);
+  return cudaGetLastError();
+}
+template <int QUANT, int CPL, int PT>
+cudaError_t occupancy_t(uint32_t smem_per_block, int* blocks) {
+  auto k = search_kernel<QUANT, CPL, PT>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, kWarpsPerBlock * 32, smem_per_block);
+}
+
+template <int QUANT, int CPL>
+cudaError_t dispatch_pt(int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st, int* blocks) {
+  switch (pt) {
+    case 2: return occ ? occupancy_t<QUANT, CPL, 2>(smem, blocks) : launch_t<QUANT, CPL, 2>(a, smem, grid, st);
+    case 4: return occ ? occupancy_t<QUANT, CPL, 4>(smem, blocks) : launch_t<QUANT, CPL, 4>(a, smem, grid, st);
+    case 8: return occ ? occupancy_t<QUANT, CPL, 8>(smem, blocks) : launch_t<QUANT, CPL, 8>(a, smem, grid, st);
+  }
+  return cudaErrorInvalidValue;
+}
+template <int QUANT>
+cudaError_t dispatch_cpl(int cpl, int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
+                         int* blocks) {
+  switch (cpl) {
+    case 1: return dispatch_pt<QUANT, 1>(pt, occ, a, smem, grid, st, blocks);
+    case 2: return dispatch_pt<QUANT, 2>(pt, occ, a, smem, grid, st, blocks);
+    case 4: return dispatch_pt<QUANT, 4>(pt, occ, a, smem, grid, st, blocks);
+    case 8: return dispatch_pt<QUANT, 8>(pt, occ, a, smem, grid, st, blocks);
+  }
+  return cudaErrorInvalidValue;
+}
+cudaError_t dispatch(int quant, int cpl, int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid,
+                     cudaStream_t st, int* blocks) {
+  return quant == 0 ? dispatch_cpl<0>(cpl, pt, occ, a, smem, grid, st, blocks)
+                    : dispatch_cpl<1>(cpl, pt, occ, a, smem, grid, st, blocks);
+}
+
+constexpr uint32_t kMaxEf = 256;
+constexpr uint32_t kMaxDimSq4 = 256;
+constexpr uint32_t kMaxDimSq8 = 128;
+constexpr uint32_t kMaxR = 128;
+constexpr uint32_t kMaxNavK = 32;
+
+// AdaptiveEf::estimate_ef for every rank 0..S (src/graph/adaptive_ef.rs:340-359),
+// evaluated on the host with the platform powf like the reference.
+std::vector<uint32_t> ef_table(uint32_t S, uint32_t min_ef, uint32_t max_ef, float gamma) {
+  std::vector<uint32_t> t(S + 1);
+  for (uint32_t r = 0; r <= S; ++r) {
+    float pct = (float)r / (float)S;
+    float shaped = powf(pct, gamma);
+    float ef = std::fma(shaped, (float)(max_ef - min_ef), (float)min_ef);
+    float rd = std::round(ef);
+    uint32_t v = 0;
+    if (rd > 0.0f) v = rd >= 4294967295.0f ? 0xFFFFFFFFu : (uint32_t)rd;
+    t[r] = v;
+  }
+  return t;
+}
+
+struct Plan {
+  int quant, cpl, pt, hash_bits;
+  uint32_t ef_cap;
+  uint32_t smem_warp, smem_block;
+  std::vector<uint32_t> table;
+  uint32_t ef_mid;
+};
+
+int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
+  if (!p) return fail(RAVEN_EINVAL, "null search params");
+  if (p->quant != RAVEN_QUANT_SQ4 && p->quant != RAVEN_QUANT_SQ8) return fail(RAVEN_EINVAL, "unknown quant");
+  if (!ix->has_q[p->quant])
+    return fail(RAVEN_ESTATE, p->quant == 0 ? "search_sq4 requires with_sq4() first (index uploaded without SQ4)"
+                                            : "search_sq8 requires with_sq8() first (index uploaded without SQ8)");
+  if (p->k == 0) return fail(RAVEN_EINVAL, "k must be >= 1");
+  pl->quant = p->quant;
+  pl->cpl = (int)(ix->q_stride[p->quant] / 16);
+  uint32_t ef_cap;
+  if (p->adaptive) {
+    if (p->max_ef < p->min_ef) return fail(RAVEN_EINVAL, "max_ef must be >= min_ef");
+    uint32_t S = (uint32_t)ix->h_samples.size();
+    if (S == 0 && !ix->has_nav) return fail(RAVEN_ESTATE, "AdaptiveEf requires layered nav samples");
+    pl->table = ef_table(S, p->min_ef, p->max_ef, p->gamma);
+    pl->ef_mid = p->min_ef + (p->max_ef - p->min_ef) / 2;  // usize::midpoint
+    ef_cap = pl->ef_mid;
+    if (S > 1)
+      for (uint32_t v : pl->table) ef_cap = std::max(ef_cap, v);
+    ef_cap = std::max(ef_cap, p->k);
+    if (S <= 1 && std::max(pl->ef_mid, p->k) == 0) return fail(RAVEN_EINVAL, "ef must be >= 1");
+  } else {
+    if (p->ef == 0) return fail(RAVEN_EINVAL, "ef must be >= 1");
+    ef_cap = p->ef;
+  }
+  if (ef_cap > kMaxEf) return fail(RAVEN_ELIMIT, "ef above the engine limit of 256");
+  pl->ef_cap = ef_cap;
+  pl->pt = ef_cap <= 64 ? 2 : ef_cap <= 128 ? 4 : 8;
+  uint32_t hb = ix->hash_bits_override;
+  if (hb == 0) {
+    uint32_t want = next_pow2(std::max<uint32_t>(1024, ef_cap * 48));
+    hb = 0;
+    while ((1u << hb) < want) ++hb;
+    hb = std::min<uint32_t>(hb, 13);
+  }
+  pl->hash_bits = (int)hb;
+  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pt, hb);
+  pl->smem_block = pl->smem_warp * kWarpsPerBlock;
+  return RAVEN_OK;
+}
+
+// Runs the search (or the nav-only descent) for device buffers.
+int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
+               const raven_search_outputs* o, cudaStream_t st, int nav_only) {
+  Plan pl;
+  raven_search_params nav_p{};
+  if (nav_only) {
+    nav_p.quant = ix->has_q[0] ? 0 : 1;
+    nav_p.ef = 1;
+    nav_p.k = 1;
+    p = &nav_p;
+  }
+  int rc = make_plan(ix, p, &pl);
+  if (rc) return rc;
+  if (nq == 0) return RAVEN_OK;
+  if (!o || !o->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
+  CU(cudaSetDevice(ix->device));
+  int blocks_per_sm = 0;
+  CU(dispatch(pl.quant, pl.cpl, pl.pt, true, SearchArgs{}, pl.smem_block, 0, st, &blocks_per_sm));
+  if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
+  uint64_t grid64 = (uint64_t)blocks_per_sm * ix->num_sms;
+  uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  int grid = (int)std::max<uint64_t>(1, std::min(grid64, need));
+  const uint64_t slots = (uint64_t)grid * kWarpsPerBlock;
+  // per-call scratch: work counter, spill tables, ef table (stream ordered)
+  const size_t spill_bytes = (size_t)slots << ix->spill_bits << 2;
+  const size_t table_bytes = pl.table.size() * 4;
+  size_t total = 256 + spill_bytes + ((table_bytes + 255) & ~(size_t)255);
+  uint8_t* scratch = nullptr;
+  CU(cudaMallocAsync((void**)&scratch, total, st));
+  unsigned long long* counter = (unsigned long long*)scratch;
+  uint32_t* spill = (uint32_t*)(scratch + 256);
+  uint32_t* table = (uint32_t*)(scratch + 256 + spill_bytes);
+  cudaError_t e = cudaMemsetAsync(counter, 0, 8, st);
+  if (e == cudaSuccess && table_bytes)
+    e = cudaMemcpyAsync(table, pl.table.data(), table_bytes, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) {
+    cudaFreeAsync(scratch, st);
+    return fail(RAVEN_ECUDA, std::string("scratch setup: ") + cudaGetErrorString(e));
+  }
+  SearchArgs a{};
+  a.vec = ix->d_vec;
+  a.dim = ix->dim;
+  a.dim_pad = ix->dim_pad;
+  a.adj = ix->d_adj;
+  a.r_pad = ix->r_pad;
+  a.codes = ix->d_codes[pl.quant];
+  a.code_stride = ix->q_stride[pl.quant];
+  a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
+  a.q_neg = ix->d_qparams[pl.quant] + 4 * ix->dim;
+  a.levels = pl.quant == 0 ? 15.0f : 255.0f;
+  a.entry = ix->entry;
+  a.nav = ix->has_nav ? 1 : 0;
+  a.nav_entry = ix->nav_entry;
+  a.nav_max_level = ix->nav_max_level;
+  a.nav_k = ix->nav_k;
+  a.nav_slot = ix->d_nav_slot;
+  a.nav_off = ix->d_nav_off;
+  a.nav_edges = ix->d_nav_edges;
+  a.adaptive = p->adaptive ? 1 : 0;
+  a.samples = ix->d_samples;
+  a.n_samples = (uint32_t)ix->h_samples.size();
+  a.ef_table = table;
+  a.ef_mid = pl.ef_mid;
+  a.ef_fixed = p->ef;
+  a.k = p->k;
+  a.rr = std::max<uint32_t>(p->rerank_factor, 1);
+  a.hash_bits = pl.hash_bits;
+  a.spill_bits = ix->spill_bits;
+  a.spill = spill;
+  a.smem_per_warp = pl.smem_warp;
+  a.queries = d_q;
+  a.nq = nq;
+  a.ids = o->ids;
+  a.dists = o->dists;
+  a.counts = o->counts;
+  a.visited = o->visited;
+  a.ef_used = o->ef_used;
+  a.status = o->status;
+  a.n_nav = o->n_nav;
+  a.expansions = o->expansions;
+  a.history = o->history;
+  a.hist_cap = o->history ? o->history_cap : 0;
+  a.hist_len = o->history_len;
+  a.counter = counter;
+  a.nav_only = nav_only;
+  e = dispatch(pl.quant, pl.cpl, pl.pt, false, a, pl.smem_block, grid, st, nullptr);
+  cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
+  return RAVEN_OK;
+}
+
+template <class T>
+int dev_alloc_copy(T** dst, const T* src, size_t count) {
+  CU(cudaMalloc((void**)dst, std::max<size_t>(count, 1) * sizeof(T)));
+  if (count) CU(cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyHostToDevice));
+  return RAVEN_OK;
+}
+
+void free_index(raven_index* ix) {
+  if (!ix) return;
+  cudaSetDevice(ix->device);
+  cudaFree(ix->d_vec);
+  cudaFree(ix->d_adj);
+  for (int q = 0; q < 2; ++q) {
+    cudaFree(ix->d_codes[q]);
+    cudaFree(ix->d_qparams[q]);
+  }
+  cudaFree(ix->d_nav_slot);
+  cudaFree(ix->d_nav_off);
+  cudaFree(ix->d_nav_edges);
+  cudaFree(ix->d_samples);
+  if (ix->stream) cudaStreamDestroy(ix->stream);
+  delete ix;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char* raven_last_error(void) { return g_err.c_str(); }
+const char* raven_version(void) { return "raven-b200 0.1 (sm_100a)"; }
+
+void raven_limits(raven_limits_t* out) {
+  if (!out) return;
+  out->max_ef = kMaxEf;
+  out->max_dim = kMaxDimSq4;
+  out->max_r = kMaxR;
+  out->max_nav_k = kMaxNavK;
+}
+
+int raven_graph_build(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg,
+                      raven_graph** out) {
+  if (!out || (!vectors && n) || !cfg) return fail(RAVEN_EINVAL, "null argument");
+  raven::BuildConfig c;
+  c.alpha = cfg->alpha;
+  c.l_build = cfg->l_build;
+  c.r_max = cfg->r_max;
+  c.r_soft = cfg->r_soft;
+  c.max_iterations = cfg->max_iterations;
+  c.saturate = cfg->saturate != 0;
+  c.enable_layered_nav = cfg->layered_nav != 0;
+  c.nav_m = cfg->nav_m;
+  c.directional = cfg->directional != 0;
+  c.seed = cfg->seed;
+  c.threads = cfg->threads;
+  c.verbose = cfg->verbose;
+  if (c.nav_m < 2) return fail(RAVEN_EINVAL, "nav_m must be >= 2");
+  raven_graph* g = new raven_graph();
+  std::string err;
+  int rc = raven::build_vamana(vectors, n, dim, c, &g->g, &err);
+  if (rc) {
+    delete g;
+    return fail(rc, err);
+  }
+  *out = g;
+  return RAVEN_OK;
+}
+
+int raven_graph_load_bytes(const void* bytes, size_t len, raven_graph** out) {
+  if (!out || (!bytes && len)) return fail(RAVEN_EINVAL, "null argument");
+  raven_graph* g = new raven_graph();
+  std::string err;
+  int rc = raven::parse_annx((const uint8_t*)bytes, len, &g->g, &err);
+  if (rc) {
+    delete g;
+    return fail(rc, err);
+  }
+  *out = g;
+  return RAVEN_OK;
+}
+
+int raven_graph_load(const char* path, raven_graph** out) {
+  if (!path || !out) return fail(RAVEN_EINVAL, "null argument");
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return fail(RAVEN_EIO, std::string("cannot open ") + path);
+  std::vector<uint8_t> bytes((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+  return raven_graph_load_bytes(bytes.data(), bytes.size(), out);
+}
+
+int raven_graph_save(const raven_graph* g, const char* path) {
+  if (!g || !path) return fail(RAVEN_EINVAL, "null argument");
+  std::vector<uint8_t> bytes = raven::serialize_annx(g->g);
+  std::ofstream f(path, std::ios::binary);
+  if (!f) return fail(RAVEN_EIO, std::string("cannot open ") + path + " for writing");
+  f.write((const char*)bytes.data(), (std::streamsize)bytes.size());
+  if (!f) return fail(RAVEN_EIO, std::string("write failed: ") + path);
+  return RAVEN_OK;
+}
+
+void raven_graph_free(raven_graph* g) { delete g; }
+
+int raven_graph_info(const raven_graph* g, raven_graph_info_t* out) {
+  if (!g || !out) return fail(RAVEN_EINVAL, "null argument");
+  out->n = g->g.n;
+  out->dim = g->g.dim;
+  out->r_max = g->g.r_max;
+  out->entry_point = g->g.entry;
+  out->has_nav = g->g.nav.present ? 1 : 0;
+  out->nav_entry = g->g.nav.entry;
+  out->nav_max_level = g->g.nav.max_level;
+  out->nav_k = g->g.nav.k;
+  uint64_t c = 0;
+  for (auto& l : g->g.nav.upper) c += !l.empty();
+  out->nav_upper_nodes = c;
+  return RAVEN_OK;
+}
+
+int raven_graph_neighbors(const raven_graph* g, uint32_t node, uint32_t* out, uint32_t cap, uint32_t* deg) {
+  if (!g || node >= g->g.n) return fail(RAVEN_EINVAL, "node out of range");
+  uint32_t d = g->g.degrees[node];
+  const uint32_t* row = g->g.main_block.data() + (size_t)node * g->g.r_max;
+  for (uint32_t i = 0; i < d && i < cap; ++i) out[i] = row[i];
+  if (deg) *deg = d;
+  return RAVEN_OK;
+}
+
+int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, uint32_t dim,
+                       const raven_upload_options* opt, raven_index** out) {
+  if (!gr || !out || (!vectors && n)) return fail(RAVEN_EINVAL, "null argument");
+  const raven::HostGraph& g = gr->g;
+  if (n != g.n) return fail(RAVEN_EINVAL, "vector count does not match the graph");
+  if (dim != g.dim) return fail(RAVEN_EINVAL, "dim mismatch: expected " + std::to_string(g.dim) + ", got " + std::to_string(dim));
+  if (n == 0) return fail(RAVEN_EINVAL, "empty index");
+  if (n >= 0x7FFFFFFFull) return fail(RAVEN_ELIMIT, "node ids must fit in 31 bits");
+  raven_upload_options o{0, 1, 0, 0};
+  if (opt) o = *opt;
+  if (g.r_max > kMaxR) return fail(RAVEN_ELIMIT, "graph degree above the engine limit of 128");
+  if (o.build_sq4 && dim > kMaxDimSq4) return fail(RAVEN_ELIMIT, "dim above the SQ4 engine limit of 256");
+  if (o.build_sq8 && dim > kMaxDimSq8) return fail(RAVEN_ELIMIT, "dim above the SQ8 engine limit of 128");
+  // validate ids before any device work (ids index device arrays)
+  if (g.entry >= n) return fail(RAVEN_EFORMAT, "entry point out of range");
+  for (size_t i = 0; i < g.main_block.size(); ++i)
+    if (g.main_block[i] != raven::kSentinel && g.main_block[i] >= n)
+      return fail(RAVEN_EFORMAT, "adjacency id out of range at slot " + std::to_string(i));
+  const bool nav = g.nav.present;
+  if (nav) {
+    if (g.nav.entry >= n) return fail(RAVEN_EFORMAT, "navigation entry out of range");
+    if (g.nav.max_level > 0 && (g.nav.k == 0 || g.nav.k > kMaxNavK))
+      return fail(RAVEN_ELIMIT, "navigation degree K must be in 1..32");
+    if (g.nav.upper.size() > n) return fail(RAVEN_EFORMAT, "navigation covers more nodes than the graph");
+    for (auto& l : g.nav.upper)
+      for (uint32_t v : l)
+        if (v >= n) return fail(RAVEN_EFORMAT, "navigation edge out of range");
+  }
+  int dev_count = 0;
+  CU(cudaGetDeviceCount(&dev_count));
+  if (o.device < 0 || o.device >= dev_count) return fail(RAVEN_EINVAL, "no such CUDA device");
+  CU(cudaSetDevice(o.device));
+  raven_index* ix = new raven_index();
+  ix->device = o.device;
+  auto bail = [&](int rc) {
+    free_index(ix);
+    return rc;
+  };
+  if (cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, o.device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(fail(RAVEN_ECUDA, "device query / stream creation failed"));
+  {
+    // per-call scratch comes from the device's stream-ordered pool; keep freed
+    // blocks cached instead of returning them to the driver at every sync
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, o.device) == cudaSuccess) {
+      uint64_t thr = ~0ull;
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+    }
+  }
+  ix->n = n;
+  ix->dim = dim;
+  ix->dim_pad = (dim + 15) & ~15u;
+  ix->r_max = (uint32_t)g.r_max;
+  ix->r_pad = (ix->r_max + 31) & ~31u;
+  ix->entry = g.entry;
+  int rc;
+  if ((rc = dev_alloc_copy(&ix->d_vec, vectors, n * (size_t)dim))) return bail(rc);
+  // adjacency, padded to r_pad
+  if (ix->r_pad == ix->r_max) {
+    if ((rc = dev_alloc_copy(&ix->d_adj, g.main_block.data(), g.main_block.size()))) return bail(rc);
+  } else {
+    std::vector<uint32_t> pad((size_t)n * ix->r_pad, raven::kSentinel);
+    for (uint64_t i = 0; i < n; ++i)
+      std::memcpy(pad.data() + i * ix->r_pad, g.main_block.data() + i * g.r_max, g.r_max * 4);
+    if ((rc = dev_alloc_copy(&ix->d_adj, pad.data(), pad.size()))) return bail(rc);
+  }
+  // quantisers: fit on the host (exact sequential min/max semantics), encode on the device
+  for (int q = 0; q < 2; ++q) {
+    if (!(q == 0 ? o.build_sq4 : o.build_sq8)) continue;
+    uint32_t bytes = q == 0 ? (dim + 1) / 2 : dim;
+    uint32_t stride = std::max<uint32_t>(16, next_pow2(bytes));
+    ix->q_stride[q] = stride;
+    ix->h_qparams[q].resize(5 * (size_t)dim);
+    raven::sq_fit_host(vectors, n, dim, q == 0 ? 15.0f : 255.0f, ix->h_qparams[q].data(), 0);
+    if ((rc = dev_alloc_copy(&ix->d_qparams[q], ix->h_qparams[q].data(), ix->h_qparams[q].size()))) return bail(rc);
+    if (cudaMalloc((void**)&ix->d_codes[q], (size_t)n * stride) != cudaSuccess)
+      return bail(fail(RAVEN_ENOMEM, "code allocation failed"));
+    encode_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(ix->d_vec, n, dim, ix->d_qparams[q] + 3 * dim,
+                                                          ix->d_qparams[q] + 4 * dim, q == 0 ? 15.0f : 255.0f,
+                                                          q == 0, stride, (uint32_t*)ix->d_codes[q]);
+    if (cudaGetLastError() != cudaSuccess) return bail(fail(RAVEN_ECUDA, "encode launch failed"));
+    ix->has_q[q] = true;
+  }
+  // navigation layers
+  if (nav) {
+    ix->has_nav = true;
+    ix->nav_entry = g.nav.entry;
+    ix->nav_max_level = g.nav.max_level;
+    ix->nav_k = g.nav.k;
+    std::vector<uint32_t> slot(n, raven::kSentinel), off{0}, edges;
+    for (size_t i = 0; i < g.nav.upper.size(); ++i) {
+      if (g.nav.upper[i].empty()) continue;
+      slot[i] = (uint32_t)(off.size() - 1);
+      edges.insert(edges.end(), g.nav.upper[i].begin(), g.nav.upper[i].end());
+      off.push_back((uint32_t)edges.size());
+    }
+    if ((rc = dev_alloc_copy(&ix->d_nav_slot, slot.data(), slot.size()))) return bail(rc);
+    if ((rc = dev_alloc_copy(&ix->d_nav_off, off.data(), off.size()))) return bail(rc);
+    if ((rc = dev_alloc_copy(&ix->d_nav_edges, edges.data(), edges.size()))) return bail(rc);
+  }
+  if (cudaStreamSynchronize(ix->stream) != cudaSuccess) return bail(fail(RAVEN_ECUDA, "upload failed"));
+  // AdaptiveEf samples: nav.initialize distances of base vectors 0..min(n,2000)
+  if (o.build_adaptive) {
+    if (!nav) return bail(fail(RAVEN_ESTATE, "AdaptiveEf requires layered nav (enable_layered_nav=true)"));
+    if (!ix->has_q[0] && !ix->has_q[1]) return bail(fail(RAVEN_ESTATE, "AdaptiveEf needs a quantiser"));
+    uint32_t S = (uint32_t)std::min<uint64_t>(n, 2000);
+    uint32_t* d_e = nullptr;
+    float* d_d = nullptr;
+    if (cudaMalloc((void**)&d_e, S * 4) != cudaSuccess || cudaMalloc((void**)&d_d, S * 4) != cudaSuccess) {
+      cudaFree(d_e);
+      return bail(fail(RAVEN_ENOMEM, "sample buffers"));
+    }
+    raven_search_outputs so{};
+    so.ids = d_e;
+    so.dists = d_d;
+    rc = run_search(ix, ix->d_vec, S, nullptr, &so, ix->stream, 1);
+    ix->h_samples.resize(S);
+    cudaError_t e = rc ? cudaSuccess : cudaMemcpyAsync(ix->h_samples.data(), d_d, S * 4, cudaMemcpyDeviceToHost, ix->stream);
+    cudaError_t e2 = cudaStreamSynchronize(ix->stream);
+    cudaFree(d_e);
+    cudaFree(d_d);
+    if (rc) return bail(rc);
+    if (e != cudaSuccess || e2 != cudaSuccess) return bail(fail(RAVEN_ECUDA, "sample distances"));
+    std::sort(ix->h_samples.begin(), ix->h_samples.end());
+    if ((rc = dev_alloc_copy(&ix->d_samples, ix->h_samples.data(), ix->h_samples.size()))) return bail(rc);
+  }
+  *out = ix;
+  return RAVEN_OK;
+}
+
+int raven_index_free(raven_index* ix) {
+  free_index(ix);
+  return RAVEN_OK;
+}
+
+int raven_index_adaptive_samples(const raven_index* ix, float* out, uint32_t cap, uint32_t* n_out) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  uint32_t S = (uint32_t)ix->h_samples.size();
+  if (out)
+    for (uint32_t i = 0; i < S && i < cap; ++i) out[i] = ix->h_samples[i];
+  if (n_out) *n_out = S;
+  return RAVEN_OK;
+}
+
+int raven_index_sq_params(const raven_index* ix, int32_t quant, float* out5dim) {
+  if (!ix || !out5dim || (quant != 0 && quant != 1)) return fail(RAVEN_EINVAL, "bad argument");
+  if (!ix->has_q[quant]) return fail(RAVEN_ESTATE, "quantiser not built");
+  std::memcpy(out5dim, ix->h_qparams[quant].data(), ix->h_qparams[quant].size() * 4);
+  return RAVEN_OK;
+}
+
+int raven_index_codes(const raven_index* ix, int32_t quant, uint8_t* out, uint64_t cap_bytes) {
+  if (!ix || !out || (quant != 0 && quant != 1)) return fail(RAVEN_EINVAL, "bad argument");
+  if (!ix->has_q[quant]) return fail(RAVEN_ESTATE, "quantiser not built");
+  const uint32_t bytes = quant == 0 ? (ix->dim + 1) / 2 : ix->dim;
+  if (cap_bytes < ix->n * bytes) return fail(RAVEN_EINVAL, "output buffer too small");
+  CU(cudaSetDevice(ix->device));
+  CU(cudaMemcpy2D(out, bytes, ix->d_codes[quant], ix->q_stride[quant], bytes, ix->n, cudaMemcpyDeviceToHost));
+  return RAVEN_OK;
+}
+
+int raven_search_batch_device(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
+                              const raven_search_outputs* d_out, void* stream) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  if (nq && !d_q) return fail(RAVEN_EINVAL, "null queries");
+  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  return run_search(ix, d_q, nq, p, d_out, st, 0);
+}
+
+int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven_search_params* p,
+                       const raven_search_outputs* out, void* stream) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  if (!out || !out->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
+  if (!p) return fail(RAVEN_EINVAL, "null search params");
+  if (nq == 0) return RAVEN_OK;
+  if (!q) return fail(RAVEN_EINVAL, "null queries");
+  CU(cudaSetDevice(ix->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  const uint64_t k = p->k;
+  const uint64_t hc = out->history ? out->history_cap : 0;
+  // one device block for queries + every requested output
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  const size_t o_q = take(nq * ix->dim * 4), o_ids = take(nq * k * 4);
+  const size_t o_d = out->dists ? take(nq * k * 4) : 0;
+  const size_t o_c = out->counts ? take(nq * 4) : 0, o_v = out->visited ? take(nq * 4) : 0;
+  const size_t o_e = out->ef_used ? take(nq * 4) : 0, o_s = out->status ? take(nq * 4) : 0;
+  const size_t o_n = out->n_nav ? take(nq * 4) : 0, o_x = out->expansions ? take(nq * 4) : 0;
+  const size_t o_h = hc ? take(nq * hc * 4) : 0, o_hl = hc ? take(nq * 4) : 0;
+  uint8_t* buf = nullptr;
+  CU(cudaMallocAsync((void**)&buf, off, st));
+  raven_search_outputs d{};
+  d.ids = (uint32_t*)(buf + o_ids);
+  d.dists = out->dists ? (float*)(buf + o_d) : nullptr;
+  d.counts = out->counts ? (uint32_t*)(buf + o_c) : nullptr;
+  d.visited = out->visited ? (uint32_t*)(buf + o_v) : nullptr;
+  d.ef_used = out->ef_used ? (uint32_t*)(buf + o_e) : nullptr;
+  d.status = out->status ? (int32_t*)(buf + o_s) : nullptr;
+  d.n_nav = out->n_nav ? (uint32_t*)(buf + o_n) : nullptr;
+  d.expansions = out->expansions ? (uint32_t*)(buf + o_x) : nullptr;
+  d.history = hc ? (uint32_t*)(buf + o_h) : nullptr;
+  d.history_cap = (uint32_t)hc;
+  d.history_len = hc ? (uint32_t*)(buf + o_hl) : nullptr;
+  int rc = RAVEN_OK;
+  cudaError_t e = cudaMemcpyAsync(buf + o_q, q, nq * ix->dim * 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && hc) e = cudaMemsetAsync(d.history, 0, nq * hc * 4, st);  // entries past history_len read 0
+  if (e == cudaSuccess) rc = run_search(ix, (const float*)(buf + o_q), nq, p, &d, st, 0);
+  auto back = [&](void* dst, const void* src, size_t bytes) {
+    if (dst && e == cudaSuccess) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st);
+  };
+  if (rc == RAVEN_OK && e == cudaSuccess) {
+    back(out->ids, d.ids, nq * k * 4);
+    back(out->dists, d.dists, nq * k * 4);
+    back(out->counts, d.counts, nq * 4);
+    back(out->visited, d.visited, nq * 4);
+    back(out->ef_used, d.ef_used, nq * 4);
+    back(out->status, d.status, nq * 4);
+    back(out->n_nav, d.n_nav, nq * 4);
+    back(out->expansions, d.expansions, nq * 4);
+    if (hc) {
+      back(out->history, d.history, nq * hc * 4);
+      back(out->history_len, d.history_len, nq * 4);
+    }
+  }
+  cudaFreeAsync(buf, st);
+  cudaError_t es = cudaStreamSynchronize(st);
+  if (rc) return rc;
+  if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search copies: ") + cudaGetErrorString(e));
+  if (es != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search: ") + cudaGetErrorString(es));
+  return RAVEN_OK;
+}
+
+int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint32_t k, uint32_t* d_ids,
+                           float* d_dists, void* stream) {
+  if (!ix || (!d_q && nq) || !d_ids || !d_dists) return fail(RAVEN_EINVAL, "null argument");
+  if (k == 0 || k > KMAXK) return fail(RAVEN_ELIMIT, "k must be in 1..32");
+  if (nq == 0) return RAVEN_OK;
+  CU(cudaSetDevice(ix->device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  const uint64_t qblocks = (nq + KQ - 1) / KQ;
+  uint64_t splits = std::max<uint64_t>(1, (uint64_t)ix->num_sms * 4 / std::max<uint64_t>(qblocks, 1));
+  splits = std::min<uint64_t>(splits, (ix->n + KB - 1) / KB);
+  splits = std::min<uint64_t>(splits, 64);
+  uint64_t split_rows = (ix->n + splits - 1) / splits;
+  split_rows = (split_rows + KB - 1) / KB * KB;
+  splits = (ix->n + split_rows - 1) / split_rows;
+  uint8_t* tmp = nullptr;
+  const size_t per = splits * nq * k;
+  CU(cudaMallocAsync((void**)&tmp, per * 8, st));
+  uint32_t* ti = (uint32_t*)tmp;
+  float* td = (float*)(tmp + per * 4);
+  dim3 grid((unsigned)qblocks, (unsigned)splits);
+  knn_tile_kernel<<<grid, 256, 0, st>>>(ix->d_vec, ix->n, d_q, nq, ix->dim, k, split_rows, ti, td);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    knn_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(ti, td, (uint32_t)splits, nq, k, d_ids, d_dists);
+    e = cudaGetLastError();
+  }
+  cudaFreeAsync(tmp, st);
+  if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("knn: ") + cudaGetErrorString(e));
+  return RAVEN_OK;
+}
+
+int raven_merge_topk_device(const uint32_t* d_ids, const float* d_dists, const uint32_t* d_counts, uint32_t n_shards,
+                            uint64_t nq, uint32_t k, uint64_t shard_size, uint32_t* d_out_ids, float* d_out_dists,
+                            uint32_t* d_out_counts, void* stream) {
+  if (!d_ids || !d_dists || !d_out_ids || !d_out_dists) return fail(RAVEN_EINVAL, "null argument");
+  if (n_shards == 0 || k == 0) return fail(RAVEN_EINVAL, "n_shards and k must be >= 1");
+  if (nq == 0) return RAVEN_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(d_ids, d_dists, d_counts, n_shards, nq, k,
+                                                                        shard_size, d_out_ids, d_out_dists,
+                                                                        d_out_counts);
+  CU(cudaGetLastError());
+  return RAVEN_OK;
+}
+
+// Tuning hooks (benchmark sweeps): 0 keeps the default.
+int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bits) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  if (hash_bits && (hash_bits < 8 || hash_bits > 14)) return fail(RAVEN_EINVAL, "hash_bits must be in 8..14");
+  if (spill_bits && (spill_bits < 10 || spill_bits > 20)) return fail(RAVEN_EINVAL, "spill_bits must be in 10..20");
+  ix->hash_bits_override = hash_bits;
+  if (spill_bits) ix->spill_bits = spill_bits;
+  return RAVEN_OK;
+}
+
+}  // extern "C"
