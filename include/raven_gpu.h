@@ -152,11 +152,11 @@ typedef struct {
 } raven_search_outputs;
 
 /* GraphSearcher::batch_search (src/graph/vamana.rs:1983-2095) with host
- * buffers: copies queries in, runs on `stream` (NULL = the index's own
- * stream), copies outputs back and synchronises. */
+ * buffers: copies queries in, runs on `stream` (a cudaStream_t; NULL = the
+ * CUDA default stream), copies outputs back and synchronises that stream. */
 RAVEN_API int raven_search_batch(raven_index* ix, const float* queries, uint64_t nq, const raven_search_params* p,
                        const raven_search_outputs* out, void* stream);
-/* Same with device buffers; asynchronous on `stream`. */
+/* Same with device buffers; asynchronous on `stream` (NULL = the CUDA default stream). */
 RAVEN_API int raven_search_batch_device(raven_index* ix, const float* d_queries, uint64_t nq, const raven_search_params* p,
                               const raven_search_outputs* d_out, void* stream);
 

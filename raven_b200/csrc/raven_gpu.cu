@@ -43,10 +43,10 @@ struct raven_index {
   float* d_qparams[2] = {nullptr, nullptr};  // 5*dim
   std::vector<float> h_qparams[2];
   bool has_nav = false;
-  uint32_t nav_entry = 0, nav_max_level = 0, nav_k = 0;
-  uint32_t* d_nav_slot = nullptr;
-  uint32_t* d_nav_off = nullptr;
-  uint32_t* d_nav_edges = nullptr;
+  uint32_t nav_entry_h = 0, nav_max_level = 0, nav_k = 0, nav_stride_levels = 0;
+  float* d_nav_vec = nullptr;      // slots x dim, lane-major
+  uint32_t* d_nav_e = nullptr;     // slots x stride_levels x k handles
+  uint32_t* d_nav_gid = nullptr;   // slot -> global id
   std::vector<float> h_samples;
   float* d_samples = nullptr;
   // launch tuning
@@ -108,6 +108,28 @@ __global__ void encode_kernel(const float* __restrict__ v, uint64_t n, uint32_t 
   }
 }
 
+// Natural -> lane-major rows (see search_kernel.cuh).
+__global__ void permute_rows_kernel(const float* __restrict__ in, float* __restrict__ out, uint64_t n, uint32_t dim) {
+  const uint32_t C = dim / 16;
+  const uint64_t total = n * dim;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = t / dim;
+    const uint32_t d = (uint32_t)(t - r * dim);
+    out[r * dim + lane_major_pos(d, C)] = in[t];
+  }
+}
+
+// out[s] = rows[gid[s]] (row copies, any layout).
+__global__ void gather_rows_kernel(const float* __restrict__ rows, const uint32_t* __restrict__ gid, uint64_t m,
+                                   uint32_t dim, float* __restrict__ out) {
+  const uint64_t total = m * dim;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t s_ = t / dim;
+    const uint32_t d = (uint32_t)(t - s_ * dim);
+    out[t] = rows[(uint64_t)gid[s_] * dim + d];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Exact kNN (recall ground truth). Block: 64 queries x 64-row tiles of the
 // base, 256 threads, 4x4 register micro-tile of squared distances
@@ -147,7 +169,11 @@ __global__ void __launch_bounds__(256) knn_tile_kernel(const float* __restrict__
       for (int i = tid; i < KD * KQ; i += 256) {
         int qq = i / KD, dd = i % KD;
         uint64_t qi = q0 + qq;
-        qs[dd][qq] = (qi < nq && d0 + dd < dim) ? q[qi * dim + d0 + dd] : 0.0f;
+        // base rows are lane-major: fetch the query element that sits at the
+        // same position (position p < 16C holds element 16*(p%C) + p/C)
+        const uint32_t p = d0 + dd, C = dim / 16;
+        const uint32_t e = p < 16 * C ? 16 * (p % C) + p / C : p;
+        qs[dd][qq] = (qi < nq && p < dim) ? q[qi * dim + e] : 0.0f;
       }
       for (int i = tid; i < KD * KB; i += 256) {
         int bb = i / KD, dd = i % KD;
@@ -391,11 +417,13 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   pl->pt = ef_cap <= 64 ? 2 : ef_cap <= 128 ? 4 : 8;
   uint32_t hb = ix->hash_bits_override;
   if (hb == 0) {
-    uint32_t want = next_pow2(std::max<uint32_t>(1024, ef_cap * 48));
-    hb = 0;
-    while ((1u << hb) < want) ++hb;
-    hb = std::min<uint32_t>(hb, 13);
+    // 4096 slots (16 KB per warp): past 3/4 load a query continues in its
+    // global spill table, which measured cheaper than the lower residency of
+    // larger shared tables on 1M-node graphs at ef 50..140
+    hb = ef_cap <= 32 ? 11 : 12;
   }
+  // the visited table doubles as the row staging area: it must hold a row
+  while ((1u << hb) < ix->dim_pad) ++hb;
   pl->hash_bits = (int)hb;
   pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pt, hb);
   pl->smem_block = pl->smem_warp * kWarpsPerBlock;
@@ -445,6 +473,8 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.vec = ix->d_vec;
   a.dim = ix->dim;
   a.dim_pad = ix->dim_pad;
+  a.vec_c = ix->dim / 16;
+  a.vec_rem = ix->dim % 16;
   a.adj = ix->d_adj;
   a.r_pad = ix->r_pad;
   a.codes = ix->d_codes[pl.quant];
@@ -452,14 +482,24 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
   a.q_neg = ix->d_qparams[pl.quant] + 4 * ix->dim;
   a.levels = pl.quant == 0 ? 15.0f : 255.0f;
+  {
+    // largest SQ distance: (levels^2) per dimension over the padded code
+    const uint64_t per_dim = pl.quant == 0 ? 225ull : 65025ull;
+    const uint64_t dims = pl.quant == 0 ? (uint64_t)ix->q_stride[0] * 2 : (uint64_t)ix->q_stride[1];
+    const uint64_t mx = per_dim * dims;
+    uint32_t b = 0;
+    while (b < 32 && (mx >> b) != 0) ++b;
+    a.dist_bits = b;
+  }
   a.entry = ix->entry;
   a.nav = ix->has_nav ? 1 : 0;
-  a.nav_entry = ix->nav_entry;
+  a.nav_entry_h = ix->nav_entry_h;
   a.nav_max_level = ix->nav_max_level;
   a.nav_k = ix->nav_k;
-  a.nav_slot = ix->d_nav_slot;
-  a.nav_off = ix->d_nav_off;
-  a.nav_edges = ix->d_nav_edges;
+  a.nav_stride_levels = ix->nav_stride_levels;
+  a.nav_vec = ix->d_nav_vec;
+  a.nav_e = ix->d_nav_e;
+  a.nav_gid = ix->d_nav_gid;
   a.adaptive = p->adaptive ? 1 : 0;
   a.samples = ix->d_samples;
   a.n_samples = (uint32_t)ix->h_samples.size();
@@ -509,9 +549,9 @@ void free_index(raven_index* ix) {
     cudaFree(ix->d_codes[q]);
     cudaFree(ix->d_qparams[q]);
   }
-  cudaFree(ix->d_nav_slot);
-  cudaFree(ix->d_nav_off);
-  cudaFree(ix->d_nav_edges);
+  cudaFree(ix->d_nav_vec);
+  cudaFree(ix->d_nav_e);
+  cudaFree(ix->d_nav_gid);
   cudaFree(ix->d_samples);
   if (ix->stream) cudaStreamDestroy(ix->stream);
   delete ix;
@@ -678,15 +718,36 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
   ix->r_pad = (ix->r_max + 31) & ~31u;
   ix->entry = g.entry;
   int rc;
-  if ((rc = dev_alloc_copy(&ix->d_vec, vectors, n * (size_t)dim))) return bail(rc);
-  // adjacency, padded to r_pad
-  if (ix->r_pad == ix->r_max) {
-    if ((rc = dev_alloc_copy(&ix->d_adj, g.main_block.data(), g.main_block.size()))) return bail(rc);
-  } else {
+  float* d_nat = nullptr;  // natural layout, needed until codes and samples exist
+  if ((rc = dev_alloc_copy(&d_nat, vectors, n * (size_t)dim))) return bail(rc);
+  auto bail2 = [&](int code) {
+    cudaFree(d_nat);
+    return bail(code);
+  };
+  if (cudaMalloc((void**)&ix->d_vec, n * (size_t)dim * 4) != cudaSuccess)
+    return bail2(fail(RAVEN_ENOMEM, "vector allocation failed"));
+  permute_rows_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(d_nat, ix->d_vec, n, dim);
+  if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "permute launch failed"));
+  // adjacency, padded to r_pad. Each row is cut at its first SENTINEL (the
+  // degree rule of HybridBlockedCsr::from_parts, src/memory/graph.rs:234-240)
+  // and later repeats of an id are dropped: the reference marks a repeat as
+  // already visited and does nothing else with it (src/graph/vamana.rs:824-832),
+  // so the search sees the same sequence of new neighbours.
+  {
     std::vector<uint32_t> pad((size_t)n * ix->r_pad, raven::kSentinel);
-    for (uint64_t i = 0; i < n; ++i)
-      std::memcpy(pad.data() + i * ix->r_pad, g.main_block.data() + i * g.r_max, g.r_max * 4);
-    if ((rc = dev_alloc_copy(&ix->d_adj, pad.data(), pad.size()))) return bail(rc);
+    const uint32_t rm = (uint32_t)g.r_max, rp = ix->r_pad;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; ++i) {
+      const uint32_t* src = g.main_block.data() + (size_t)i * rm;
+      uint32_t* dst = pad.data() + (size_t)i * rp;
+      uint32_t m = 0;
+      for (uint32_t t = 0; t < rm && src[t] != raven::kSentinel; ++t) {
+        bool dup = false;
+        for (uint32_t u = 0; u < m; ++u) dup |= dst[u] == src[t];
+        if (!dup) dst[m++] = src[t];
+      }
+    }
+    if ((rc = dev_alloc_copy(&ix->d_adj, pad.data(), pad.size()))) return bail2(rc);
   }
   // quantisers: fit on the host (exact sequential min/max semantics), encode on the device
   for (int q = 0; q < 2; ++q) {
@@ -696,58 +757,77 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
     ix->q_stride[q] = stride;
     ix->h_qparams[q].resize(5 * (size_t)dim);
     raven::sq_fit_host(vectors, n, dim, q == 0 ? 15.0f : 255.0f, ix->h_qparams[q].data(), 0);
-    if ((rc = dev_alloc_copy(&ix->d_qparams[q], ix->h_qparams[q].data(), ix->h_qparams[q].size()))) return bail(rc);
+    if ((rc = dev_alloc_copy(&ix->d_qparams[q], ix->h_qparams[q].data(), ix->h_qparams[q].size()))) return bail2(rc);
     if (cudaMalloc((void**)&ix->d_codes[q], (size_t)n * stride) != cudaSuccess)
-      return bail(fail(RAVEN_ENOMEM, "code allocation failed"));
-    encode_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(ix->d_vec, n, dim, ix->d_qparams[q] + 3 * dim,
+      return bail2(fail(RAVEN_ENOMEM, "code allocation failed"));
+    encode_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(d_nat, n, dim, ix->d_qparams[q] + 3 * dim,
                                                           ix->d_qparams[q] + 4 * dim, q == 0 ? 15.0f : 255.0f,
                                                           q == 0, stride, (uint32_t*)ix->d_codes[q]);
-    if (cudaGetLastError() != cudaSuccess) return bail(fail(RAVEN_ECUDA, "encode launch failed"));
+    if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "encode launch failed"));
     ix->has_q[q] = true;
   }
-  // navigation layers
+  // navigation layers: every node with an upper list gets a slot; its edges
+  // are stored per level at a fixed stride (stride_levels x k, kSent padded)
+  // as handles (slot, or kGidBit|id for a target without upper list), and
+  // its vector is copied into a compact lane-major array.
   if (nav) {
     ix->has_nav = true;
-    ix->nav_entry = g.nav.entry;
     ix->nav_max_level = g.nav.max_level;
-    ix->nav_k = g.nav.k;
-    std::vector<uint32_t> slot(n, raven::kSentinel), off{0}, edges;
+    ix->nav_k = std::max<uint32_t>(g.nav.k, 1);
+    const uint32_t K = ix->nav_k;
+    std::vector<uint32_t> slot(n, raven::kSentinel), gid;
+    uint32_t levels = 0;
     for (size_t i = 0; i < g.nav.upper.size(); ++i) {
       if (g.nav.upper[i].empty()) continue;
-      slot[i] = (uint32_t)(off.size() - 1);
-      edges.insert(edges.end(), g.nav.upper[i].begin(), g.nav.upper[i].end());
-      off.push_back((uint32_t)edges.size());
+      slot[i] = (uint32_t)gid.size();
+      gid.push_back((uint32_t)i);
+      levels = std::max<uint32_t>(levels, (uint32_t)((g.nav.upper[i].size() + K - 1) / K));
     }
-    if ((rc = dev_alloc_copy(&ix->d_nav_slot, slot.data(), slot.size()))) return bail(rc);
-    if ((rc = dev_alloc_copy(&ix->d_nav_off, off.data(), off.size()))) return bail(rc);
-    if ((rc = dev_alloc_copy(&ix->d_nav_edges, edges.data(), edges.size()))) return bail(rc);
+    ix->nav_stride_levels = levels;
+    auto handle = [&](uint32_t v) { return slot[v] != raven::kSentinel ? slot[v] : (kGidBit | v); };
+    std::vector<uint32_t> e((size_t)gid.size() * levels * K, raven::kSentinel);
+    for (size_t sl = 0; sl < gid.size(); ++sl) {
+      const auto& l = g.nav.upper[gid[sl]];
+      for (size_t t = 0; t < l.size(); ++t) e[sl * levels * K + t] = handle(l[t]);
+    }
+    ix->nav_entry_h = handle(g.nav.entry);
+    if ((rc = dev_alloc_copy(&ix->d_nav_e, e.data(), e.size()))) return bail2(rc);
+    if ((rc = dev_alloc_copy(&ix->d_nav_gid, gid.data(), gid.size()))) return bail2(rc);
+    if (cudaMalloc((void**)&ix->d_nav_vec, std::max<size_t>(gid.size(), 1) * dim * 4) != cudaSuccess)
+      return bail2(fail(RAVEN_ENOMEM, "nav vector allocation failed"));
+    if (!gid.empty()) {
+      gather_rows_kernel<<<ix->num_sms * 4, 256, 0, ix->stream>>>(ix->d_vec, ix->d_nav_gid, gid.size(), dim,
+                                                                  ix->d_nav_vec);
+      if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "nav gather failed"));
+    }
   }
-  if (cudaStreamSynchronize(ix->stream) != cudaSuccess) return bail(fail(RAVEN_ECUDA, "upload failed"));
+  if (cudaStreamSynchronize(ix->stream) != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "upload failed"));
   // AdaptiveEf samples: nav.initialize distances of base vectors 0..min(n,2000)
   if (o.build_adaptive) {
-    if (!nav) return bail(fail(RAVEN_ESTATE, "AdaptiveEf requires layered nav (enable_layered_nav=true)"));
-    if (!ix->has_q[0] && !ix->has_q[1]) return bail(fail(RAVEN_ESTATE, "AdaptiveEf needs a quantiser"));
+    if (!nav) return bail2(fail(RAVEN_ESTATE, "AdaptiveEf requires layered nav (enable_layered_nav=true)"));
+    if (!ix->has_q[0] && !ix->has_q[1]) return bail2(fail(RAVEN_ESTATE, "AdaptiveEf needs a quantiser"));
     uint32_t S = (uint32_t)std::min<uint64_t>(n, 2000);
     uint32_t* d_e = nullptr;
     float* d_d = nullptr;
     if (cudaMalloc((void**)&d_e, S * 4) != cudaSuccess || cudaMalloc((void**)&d_d, S * 4) != cudaSuccess) {
       cudaFree(d_e);
-      return bail(fail(RAVEN_ENOMEM, "sample buffers"));
+      return bail2(fail(RAVEN_ENOMEM, "sample buffers"));
     }
     raven_search_outputs so{};
     so.ids = d_e;
     so.dists = d_d;
-    rc = run_search(ix, ix->d_vec, S, nullptr, &so, ix->stream, 1);
+    rc = run_search(ix, d_nat, S, nullptr, &so, ix->stream, 1);
     ix->h_samples.resize(S);
     cudaError_t e = rc ? cudaSuccess : cudaMemcpyAsync(ix->h_samples.data(), d_d, S * 4, cudaMemcpyDeviceToHost, ix->stream);
     cudaError_t e2 = cudaStreamSynchronize(ix->stream);
     cudaFree(d_e);
     cudaFree(d_d);
-    if (rc) return bail(rc);
-    if (e != cudaSuccess || e2 != cudaSuccess) return bail(fail(RAVEN_ECUDA, "sample distances"));
+    if (rc) return bail2(rc);
+    if (e != cudaSuccess || e2 != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "sample distances"));
     std::sort(ix->h_samples.begin(), ix->h_samples.end());
-    if ((rc = dev_alloc_copy(&ix->d_samples, ix->h_samples.data(), ix->h_samples.size()))) return bail(rc);
+    if ((rc = dev_alloc_copy(&ix->d_samples, ix->h_samples.data(), ix->h_samples.size()))) return bail2(rc);
   }
+  cudaFree(d_nat);
   *out = ix;
   return RAVEN_OK;
 }
@@ -787,7 +867,7 @@ int raven_search_batch_device(raven_index* ix, const float* d_q, uint64_t nq, co
                               const raven_search_outputs* d_out, void* stream) {
   if (!ix) return fail(RAVEN_EINVAL, "null index");
   if (nq && !d_q) return fail(RAVEN_EINVAL, "null queries");
-  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
   return run_search(ix, d_q, nq, p, d_out, st, 0);
 }
 
@@ -799,7 +879,7 @@ int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven
   if (nq == 0) return RAVEN_OK;
   if (!q) return fail(RAVEN_EINVAL, "null queries");
   CU(cudaSetDevice(ix->device));
-  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
   const uint64_t k = p->k;
   const uint64_t hc = out->history ? out->history_cap : 0;
   // one device block for queries + every requested output
@@ -864,7 +944,7 @@ int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint3
   if (k == 0 || k > KMAXK) return fail(RAVEN_ELIMIT, "k must be in 1..32");
   if (nq == 0) return RAVEN_OK;
   CU(cudaSetDevice(ix->device));
-  cudaStream_t st = stream ? (cudaStream_t)stream : ix->stream;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
   const uint64_t qblocks = (nq + KQ - 1) / KQ;
   uint64_t splits = std::max<uint64_t>(1, (uint64_t)ix->num_sms * 4 / std::max<uint64_t>(qblocks, 1));
   splits = std::min<uint64_t>(splits, (ix->n + KB - 1) / KB);

@@ -17,6 +17,11 @@
 // every distance tie against an entry already in the pool, and candidates of
 // one expansion tie-break by adjacency order, so merging one expansion's
 // candidates at once gives the same pool as inserting them one by one.
+//
+// f32 rows (vectors, queries) use a lane-major layout: with C = dim/16, row
+// position j*C + c holds element 16c + j (j < 16, c < C) and the dim%16 tail
+// follows unpermuted. Lane j of a half-warp then reads its whole fma chain
+// (elements j, 16+j, 32+j, ...) contiguously, in the reference's order.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -26,15 +31,19 @@ namespace raven_dev {
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr uint32_t kSent = 0xffffffffu;
 constexpr uint32_t kChecked = 0x80000000u;
+constexpr uint32_t kGidBit = 0x80000000u;  // nav handle: global id (node without upper list)
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr int kWarpsPerBlock = 4;
+constexpr int kMinBlocksPerSm = 4;  // shared memory, not registers, bounds residency
 constexpr uint32_t kNavStepLimit = 1u << 16;
 
 struct SearchArgs {
   // index
-  const float* __restrict__ vec;
+  const float* __restrict__ vec;  // n x dim, lane-major rows
   uint32_t dim;
-  uint32_t dim_pad;  // dim rounded up to 16
+  uint32_t dim_pad;  // dim rounded up to 16 (query buffer)
+  uint32_t vec_c;    // dim / 16
+  uint32_t vec_rem;  // dim % 16
   const uint32_t* __restrict__ adj;
   uint32_t r_pad;  // row stride in ids (multiple of 32)
   const uint8_t* __restrict__ codes;
@@ -43,22 +52,26 @@ struct SearchArgs {
   const float* __restrict__ q_neg;
   float levels;  // 15 (SQ4) or 255 (SQ8)
   uint32_t entry;
+  // layered navigation, slot based (see raven_gpu.cu)
   int nav;
-  uint32_t nav_entry, nav_max_level, nav_k;
-  const uint32_t* __restrict__ nav_slot;
-  const uint32_t* __restrict__ nav_off;
-  const uint32_t* __restrict__ nav_edges;
+  uint32_t nav_entry_h;  // handle of the top entry
+  uint32_t nav_max_level, nav_k, nav_stride_levels;
+  const float* __restrict__ nav_vec;     // slots x dim, lane-major
+  const uint32_t* __restrict__ nav_e;    // slots x stride_levels x k handles, kSent padded
+  const uint32_t* __restrict__ nav_gid;  // slot -> global id
+  // AdaptiveEf
   int adaptive;
   const float* __restrict__ samples;
   uint32_t n_samples;
   const uint32_t* __restrict__ ef_table;  // n_samples + 1 entries
   uint32_t ef_mid;
   uint32_t ef_fixed, k, rr;
+  uint32_t dist_bits;   // bits of the largest possible quantised distance
   uint32_t hash_bits;   // shared-memory visited table: 1 << hash_bits slots
   uint32_t spill_bits;  // global spill table per warp slot: 1 << spill_bits slots
   uint32_t* spill;
   uint32_t smem_per_warp;
-  // queries
+  // queries (natural layout)
   const float* __restrict__ queries;
   uint64_t nq;
   // outputs
@@ -77,16 +90,16 @@ struct SearchArgs {
   int nav_only;  // 1: only run the descent; write entry to ids[q], distance to dists[q]
 };
 
-// Per-warp shared-memory carve-up (byte offsets; every piece 16-byte aligned).
+// Per-warp shared-memory carve-up (every piece 16-byte aligned).
 struct WarpSmem {
-  float* qf;         // dim_pad floats
-  uint8_t* qcode;    // code_stride bytes
-  uint32_t* pool_d;  // 32*PT
-  uint32_t* pool_id; // 32*PT
-  uint32_t* cand_id; // 32
-  uint32_t* cand_d;  // 32
-  float* nd;         // 32 (navigation distances)
-  uint32_t* ht;      // 1 << hash_bits (reused as float[] by the rerank)
+  float* qf;          // dim_pad floats, lane-major
+  uint8_t* qcode;     // code_stride bytes
+  uint32_t* pool_d;   // 32*PT
+  uint32_t* pool_id;  // 32*PT
+  uint32_t* cand_id;  // 32
+  uint32_t* cand_d;   // 32
+  float* nd;          // 32
+  uint32_t* ht;       // 1 << hash_bits; also the row staging area outside the beam search
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
@@ -120,13 +133,61 @@ __device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, int pt) {
 
 __device__ inline uint32_t lanemask_lt(int lane) { return (1u << lane) - 1u; }
 
+// Position of natural element d in a lane-major row.
+__host__ __device__ inline uint32_t lane_major_pos(uint32_t d, uint32_t c_count) {
+  const uint32_t main = 16u * c_count;
+  return d < main ? (d & 15u) * c_count + (d >> 4) : d;
+}
+
 // ---------------------------------------------------------------------------
-// f32 squared L2 of the query (shared memory) against one row, computed by a
-// half-warp in the order of _mm512 code: lane j accumulates fma(d,d,acc) over
-// elements 16c+j, then the 16 lanes are reduced by the halving tree
-// (xor 8, 4, 2, 1), a masked tail is reduced the same way, result = tail+main.
-// Both half-warps run this for their own row; every lane returns the value.
+// Asynchronous global -> shared copies (cp.async; completion by wait_group,
+// a hardware wait, no spinning).
 // ---------------------------------------------------------------------------
+__device__ inline void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ inline void cp_async4(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ inline void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Stage `nrows` f32 rows (row r from row_ptr(r)) into shared memory
+// (row r at stage + r*dim). All lanes issue copies, then wait.
+template <class RowPtr>
+__device__ inline void stage_rows(float* stage, int nrows, uint32_t dim, RowPtr row_ptr, int lane) {
+  if ((dim & 3u) == 0) {
+    const uint32_t per = dim >> 2;  // 16-byte pieces per row
+    if (per <= 32 && (per & (per - 1)) == 0) {
+      // several rows per pass: lane -> (row offset, piece) by shift/mask
+      const uint32_t sh = __ffs(per) - 1;
+      const uint32_t rows_per_pass = 32u >> sh;
+      const uint32_t ro = (uint32_t)lane >> sh, o = (uint32_t)lane & (per - 1);
+      for (uint32_t r0 = 0; r0 < (uint32_t)nrows; r0 += rows_per_pass) {
+        const uint32_t r = r0 + ro;
+        if (r < (uint32_t)nrows) cp_async16(stage + r * dim + o * 4, row_ptr(r) + o * 4);
+      }
+    } else {
+      for (uint32_t r = 0; r < (uint32_t)nrows; ++r) {
+        const float* src = row_ptr(r);
+        for (uint32_t o = lane; o < per; o += 32) cp_async16(stage + r * dim + o * 4, src + o * 4);
+      }
+    }
+  } else {
+    for (uint32_t r = 0; r < (uint32_t)nrows; ++r) {
+      const float* src = row_ptr(r);
+      for (uint32_t o = lane; o < dim; o += 32) cp_async4(stage + r * dim + o, src + o);
+    }
+  }
+  cp_async_wait_all();
+  __syncwarp();
+}
+
+// Halving tree over the 16 lanes of each half-warp (xor 8, 4, 2, 1): the
+// _mm512_reduce_add_ps order.
 __device__ inline float tree16(float v) {
   v = __fadd_rn(v, __shfl_xor_sync(kFull, v, 8));
   v = __fadd_rn(v, __shfl_xor_sync(kFull, v, 4));
@@ -135,51 +196,62 @@ __device__ inline float tree16(float v) {
   return v;
 }
 
-// Two rows per half-warp (loads of both issued together). row_a/row_b may be
-// null (then that result is garbage but all lanes still join the shuffles).
-__device__ inline void hw_l2_pair(const float* __restrict__ qf, const float* __restrict__ row_a,
-                                  const float* __restrict__ row_b, uint32_t dim, int j, float* out_a,
-                                  float* out_b) {
-  const uint32_t chunks = dim >> 4, rem = dim & 15;
-  float acc_a = 0.0f, acc_b = 0.0f;
+// Squared L2 of the (lane-major) query against a lane-major row in shared
+// memory, by a half-warp (lane j = lane & 15): lane j's fma chain over
+// c = 0..C-1 then the tree; the tail is its own masked vector reduced the
+// same way; result = tail + main (src/distance/avx512.rs:31-62). All 32 lanes
+// must call (both half-warps, each with its own row).
+__device__ inline float hw_dist(const float* __restrict__ qf, const float* __restrict__ row, uint32_t C,
+                                uint32_t rem, int j) {
+  float acc = 0.0f;
+  const float* q = qf + j * C;
+  const float* r = row + j * C;
   uint32_t c = 0;
-  for (; c + 4 <= chunks; c += 4) {
-    float va[4], vb[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      va[u] = row_a ? __ldg(row_a + (c + u) * 16 + j) : 0.0f;
-      vb[u] = row_b ? __ldg(row_b + (c + u) * 16 + j) : 0.0f;
+  if ((C & 3u) == 0) {
+    for (; c < C; c += 4) {
+      const float4 qa = *(const float4*)(q + c);
+      const float4 ra = *(const float4*)(r + c);
+      float d;
+      d = __fsub_rn(qa.x, ra.x);
+      acc = __fmaf_rn(d, d, acc);
+      d = __fsub_rn(qa.y, ra.y);
+      acc = __fmaf_rn(d, d, acc);
+      d = __fsub_rn(qa.z, ra.z);
+      acc = __fmaf_rn(d, d, acc);
+      d = __fsub_rn(qa.w, ra.w);
+      acc = __fmaf_rn(d, d, acc);
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      float q = qf[(c + u) * 16 + j];
-      float da = __fsub_rn(q, va[u]);
-      float db = __fsub_rn(q, vb[u]);
-      acc_a = __fmaf_rn(da, da, acc_a);
-      acc_b = __fmaf_rn(db, db, acc_b);
+  } else {
+    for (; c < C; ++c) {
+      const float d = __fsub_rn(q[c], r[c]);
+      acc = __fmaf_rn(d, d, acc);
     }
   }
-  for (; c < chunks; ++c) {
-    float va = row_a ? __ldg(row_a + c * 16 + j) : 0.0f;
-    float vb = row_b ? __ldg(row_b + c * 16 + j) : 0.0f;
-    float q = qf[c * 16 + j];
-    float da = __fsub_rn(q, va), db = __fsub_rn(q, vb);
-    acc_a = __fmaf_rn(da, da, acc_a);
-    acc_b = __fmaf_rn(db, db, acc_b);
-  }
-  float ta = 0.0f, tb = 0.0f;
+  float tail = 0.0f;
   if (rem) {
-    float da = 0.0f, db = 0.0f;
-    if ((uint32_t)j < rem) {
-      float q = qf[chunks * 16 + j];
-      if (row_a) da = __fsub_rn(q, __ldg(row_a + chunks * 16 + j));
-      if (row_b) db = __fsub_rn(q, __ldg(row_b + chunks * 16 + j));
-    }
-    ta = tree16(__fmaf_rn(da, da, 0.0f));
-    tb = tree16(__fmaf_rn(db, db, 0.0f));
+    float d = 0.0f;
+    if ((uint32_t)j < rem) d = __fsub_rn(qf[16 * C + j], row[16 * C + j]);
+    tail = tree16(__fmaf_rn(d, d, 0.0f));
   }
-  *out_a = __fadd_rn(ta, tree16(acc_a));
-  *out_b = __fadd_rn(tb, tree16(acc_b));
+  return __fadd_rn(tail, tree16(acc));
+}
+
+// Distances of `n` rows (handles/ids in `ids` smem, resolved by row_ptr) into
+// out[0..n), staging up to `stage_rows_max` rows per round in `stage`.
+template <class RowPtr>
+__device__ inline void rows_dist(const float* qf, float* stage, uint32_t stage_rows_max, const uint32_t* ids, int n,
+                                 uint32_t dim, uint32_t C, uint32_t rem, RowPtr row_ptr, float* out, int lane) {
+  const int h = lane >> 4, j = lane & 15;
+  for (int b0 = 0; b0 < n; b0 += (int)stage_rows_max) {
+    const int nb = min((int)stage_rows_max, n - b0);
+    stage_rows(stage, nb, dim, [&](uint32_t r) { return row_ptr(ids[b0 + r]); }, lane);
+    for (int r0 = 0; r0 < nb; r0 += 2) {
+      const int r = min(r0 + h, nb - 1);
+      const float d = hw_dist(qf, stage + (size_t)r * dim, C, rem, j);
+      if (j == 0 && r0 + h < nb) out[b0 + r0 + h] = d;
+    }
+    __syncwarp();
+  }
 }
 
 // f32 -> u32 key that orders like Rust's f32::total_cmp.
@@ -199,137 +271,128 @@ __device__ inline uint32_t quantize(float v, float inv, float neg, float levels)
 }
 
 // ---------------------------------------------------------------------------
-// Navigation descent (src/graph/navigation.rs:609-653). Returns entry + f32
-// distance; counts distance evaluations exactly as the reference does (an
-// edge equal to the running node is skipped).
+// Navigation descent (src/graph/navigation.rs:609-653). Works on handles
+// (slot index, or kGidBit|id for a node without upper list). Returns the
+// entry's global id + f32 distance and counts distance evaluations exactly as
+// the reference does (an edge equal to the running node is skipped).
 // ---------------------------------------------------------------------------
-__device__ inline bool nav_descend(const SearchArgs& a, const WarpSmem& s, int lane, uint32_t* out_u,
-                                   float* out_d, uint32_t* out_evals) {
-  const int h = lane >> 4, j = lane & 15;
-  uint32_t u = a.nav_entry;
-  float du, dummy;
-  hw_l2_pair(s.qf, a.vec + (size_t)u * a.dim, nullptr, a.dim, j, &du, &dummy);
+__device__ inline bool nav_descend(const SearchArgs& a, const WarpSmem& s, float* stage, uint32_t stage_rows_max,
+                                   int lane, uint32_t* out_gid, float* out_d, uint32_t* out_evals) {
+  auto row_of = [&](uint32_t hd) -> const float* {
+    return (hd & kGidBit) ? a.vec + (size_t)(hd & ~kGidBit) * a.dim : a.nav_vec + (size_t)hd * a.dim;
+  };
+  uint32_t u = a.nav_entry_h;
+  if (lane == 0) s.cand_id[0] = u;
+  __syncwarp();
+  rows_dist(s.qf, stage, stage_rows_max, s.cand_id, 1, a.dim, a.vec_c, a.vec_rem, row_of, s.nd, lane);
+  float du = s.nd[0];
+  __syncwarp();
   uint32_t evals = 1;
   uint32_t steps = 0;
   bool ok = true;
-  if (a.nav_max_level > 0) {
-    for (int level = (int)a.nav_max_level; level >= 1 && ok; --level) {
-      while (true) {
-        if (++steps > kNavStepLimit) {
-          ok = false;
-          break;
-        }
-        uint32_t slot = a.nav_slot[u];
-        uint32_t off = 0, len = 0;
-        if (slot != kSent) {
-          off = a.nav_off[slot];
-          len = a.nav_off[slot + 1] - off;
-        }
-        uint32_t start = (uint32_t)(level - 1) * a.nav_k;
-        if (start >= len) break;
-        uint32_t cnt = min(a.nav_k, len - start);
-        uint32_t v = (uint32_t)lane < cnt ? a.nav_edges[off + start + lane] : kSent;
-        for (uint32_t e0 = 0; e0 < cnt; e0 += 4) {
-          uint32_t ea = e0 + h, eb = e0 + 2 + h;
-          uint32_t va = __shfl_sync(kFull, v, ea & 31), vb = __shfl_sync(kFull, v, eb & 31);
-          const float* ra = ea < cnt ? a.vec + (size_t)va * a.dim : nullptr;
-          const float* rb = eb < cnt ? a.vec + (size_t)vb * a.dim : nullptr;
-          float da, db;
-          hw_l2_pair(s.qf, ra, rb, a.dim, j, &da, &db);
-          if (j == 0) {
-            if (ea < cnt) s.nd[ea] = da;
-            if (eb < cnt) s.nd[eb] = db;
-          }
-        }
-        __syncwarp();
-        float d = (uint32_t)lane < cnt ? s.nd[lane] : __int_as_float(0x7f800000);
-        // key: distance bits (non-negative floats order as integers; NaN sorts
-        // after +inf and is never selected by `d < cur`) then edge index.
-        unsigned long long key = ((unsigned long long)__float_as_uint(d) << 32) | (uint32_t)lane;
-        if ((uint32_t)lane >= cnt) key = ~0ull;
-        // Running node before edge e: the argmin over edges < e if it beats du.
-        unsigned long long pre = key;
+  const uint32_t K = a.nav_k;
+  for (int level = (int)a.nav_max_level; level >= 1 && ok; --level) {
+    while (true) {
+      if (++steps > kNavStepLimit) {
+        ok = false;
+        break;
+      }
+      if ((u & kGidBit) || (uint32_t)level > a.nav_stride_levels) break;
+      const uint32_t v =
+          (uint32_t)lane < K ? a.nav_e[((size_t)u * a.nav_stride_levels + (level - 1)) * K + lane] : kSent;
+      const uint32_t sm = __ballot_sync(kFull, v == kSent);
+      const uint32_t cnt = sm ? (uint32_t)(__ffs(sm) - 1) : 32u;
+      if (cnt == 0) break;
+      if ((uint32_t)lane < cnt) s.cand_id[lane] = v;
+      __syncwarp();
+      rows_dist(s.qf, stage, stage_rows_max, s.cand_id, (int)cnt, a.dim, a.vec_c, a.vec_rem, row_of, s.nd, lane);
+      const float d = (uint32_t)lane < cnt ? s.nd[lane] : __int_as_float(0x7f800000);
+      // key: distance bits (non-negative floats order as integers; NaN sorts
+      // after +inf and is never selected by `d < cur`) then edge index.
+      unsigned long long key = ((unsigned long long)__float_as_uint(d) << 32) | (uint32_t)lane;
+      if ((uint32_t)lane >= cnt) key = ~0ull;
+      unsigned long long pre = key;  // inclusive prefix minimum
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          unsigned long long t = __shfl_up_sync(kFull, pre, o);
-          if (lane >= o && t < pre) pre = t;
-        }
-        unsigned long long excl = __shfl_up_sync(kFull, pre, 1);
-        if (lane == 0) excl = ~0ull;
-        const bool moved = excl != ~0ull && __uint_as_float((uint32_t)(excl >> 32)) < du;
-        const uint32_t excl_v = __shfl_sync(kFull, v, moved ? (int)(excl & 31) : 0);
-        const uint32_t run_u = moved ? excl_v : u;
-        const bool counted = (uint32_t)lane < cnt && v != run_u;
-        evals += __popc(__ballot_sync(kFull, counted));
-        const unsigned long long best = __shfl_sync(kFull, pre, 31);
-        const float bd = __uint_as_float((uint32_t)(best >> 32));
-        const uint32_t best_v = __shfl_sync(kFull, v, (int)(best & 31));
-        __syncwarp();
-        if (best != ~0ull && bd < du) {
-          du = bd;
-          u = best_v;
-        } else {
-          break;
-        }
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long t = __shfl_up_sync(kFull, pre, o);
+        if (lane >= o && t < pre) pre = t;
+      }
+      unsigned long long excl = __shfl_up_sync(kFull, pre, 1);
+      if (lane == 0) excl = ~0ull;
+      // running node before edge e: the argmin over earlier edges if it beat du
+      const bool moved = excl != ~0ull && __uint_as_float((uint32_t)(excl >> 32)) < du;
+      const uint32_t excl_v = __shfl_sync(kFull, v, moved ? (int)(excl & 31) : 0);
+      const uint32_t run_u = moved ? excl_v : u;
+      evals += __popc(__ballot_sync(kFull, (uint32_t)lane < cnt && v != run_u));
+      const unsigned long long best = __shfl_sync(kFull, pre, 31);
+      const float bd = __uint_as_float((uint32_t)(best >> 32));
+      const uint32_t best_v = __shfl_sync(kFull, v, (int)(best & 31));
+      __syncwarp();
+      if (best != ~0ull && bd < du) {
+        du = bd;
+        u = best_v;
+      } else {
+        break;
       }
     }
   }
-  *out_u = u;
+  *out_gid = (u & kGidBit) ? (u & ~kGidBit) : a.nav_gid[u];
   *out_d = du;
   *out_evals = evals;
   return ok;
 }
 
 // ---------------------------------------------------------------------------
-// Visited set: open addressing in shared memory; after it passes 3/4 load the
-// warp switches to its global spill table (lookups check both). Exact: every
-// id lives in exactly one table.
+// Visited set: open addressing in shared memory; past 3/4 load the warp
+// switches to its global spill table (lookups check both). Exact: every id
+// lives in exactly one table.
 // ---------------------------------------------------------------------------
 __device__ inline uint32_t hash_slot(uint32_t id, uint32_t bits) { return (id * 0x9E3779B1u) >> (32 - bits); }
 
-// Returns 1 if inserted (first visit), 0 if present. `insert` false: lookup only
-// (returns 2 if absent).
+// Bucketed open addressing: 4-slot buckets (one 16-byte read), linear over
+// buckets. Returns 1 if inserted (first visit), 0 if present. `insert`
+// false: lookup only (returns 2 if absent). `bits` = log2(slots) >= 2.
 template <bool kShared>
 __device__ inline int probe_insert(uint32_t* t, uint32_t bits, uint32_t id, bool insert) {
-  const uint32_t mask = (1u << bits) - 1u;
-  uint32_t hsl = hash_slot(id, bits);
-  for (uint32_t it = 0; it <= mask; ++it) {
-    uint32_t cur = kShared ? t[hsl] : *(volatile uint32_t*)(t + hsl);
-    if (cur == id) return 0;
-    if (cur == kEmpty) {
+  const uint32_t nb = 1u << (bits - 2);
+  uint32_t b = hash_slot(id, bits - 2);
+  for (uint32_t it = 0; it < nb; ++it) {
+    uint4 v;
+    if (kShared) {
+      v = *(const uint4*)(t + 4 * b);
+    } else {
+      v = __ldcv((const uint4*)(t + 4 * b));  // the spill table lives in L2: bypass L1
+    }
+    if (v.x == id || v.y == id || v.z == id || v.w == id) return 0;
+    const int e = v.x == kEmpty ? 0 : v.y == kEmpty ? 1 : v.z == kEmpty ? 2 : v.w == kEmpty ? 3 : -1;
+    if (e >= 0) {
       if (!insert) return 2;
-      uint32_t old = atomicCAS(t + hsl, kEmpty, id);
+      const uint32_t old = atomicCAS(t + 4 * b + e, kEmpty, id);
       if (old == kEmpty) return 1;
       if (old == id) return 0;
+      --it;  // lost the slot to another lane: re-read this bucket
+      continue;
     }
-    hsl = (hsl + 1) & mask;
+    b = (b + 1) & (nb - 1);
   }
   return insert ? 3 : 2;  // table full (not reached: load is capped at 3/4)
 }
 
-// Ascending bitonic sort of one u32 per lane.
-__device__ inline uint32_t bitonic32(uint32_t key, int lane) {
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      uint32_t p = __shfl_xor_sync(kFull, key, j);
-      bool up = (lane & k) == 0;
-      bool lower = (lane & j) == 0;
-      key = (lower == up) ? min(key, p) : max(key, p);
-    }
-  }
-  return key;
-}
-
 __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, int lane) {
   for (int base = from & ~31; base < sz; base += 32) {
-    int p = base + lane;
-    bool ok = p >= from && p < sz && !(pool_id[p] & kChecked);
-    uint32_t m = __ballot_sync(kFull, ok);
+    const int p = base + lane;
+    const bool ok = p >= from && p < sz && !(pool_id[p] & kChecked);
+    const uint32_t m = __ballot_sync(kFull, ok);
     if (m) return base + __ffs(m) - 1;
   }
   return sz;
+}
+
+// dot product of 4 unsigned bytes (a) with 4 signed bytes (b), plus c.
+__device__ inline int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 // Integer SQ distance partial for one 16-byte chunk.
@@ -337,27 +400,34 @@ template <int QUANT>
 struct QChunk;
 
 template <>
-struct QChunk<0> {  // SQ4: nibbles; per byte (q|0x80) - b never borrows, ^0x80 gives signed q-b
-  uint32_t lo_or[4], hi_or[4];
+struct QChunk<0> {  // SQ4: sum (q-x)^2 = sum q^2 + sum x (x - 2q), nibbles unpacked to bytes
+  int m2q_lo[4], m2q_hi[4];  // -2q per byte (signed)
+  int qq;                    // sum of q^2 over this lane's 32 nibbles
   __device__ inline void load(const uint8_t* qcode, int chunk) {
-    uint4 q = *(const uint4*)(qcode + chunk * 16);
-    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    const uint4 q = *(const uint4*)(qcode + chunk * 16);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    qq = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      lo_or[i] = (w[i] & 0x0F0F0F0Fu) | 0x80808080u;
-      hi_or[i] = ((w[i] >> 4) & 0x0F0F0F0Fu) | 0x80808080u;
+      const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+      qq = __dp4a(lo, lo, (unsigned)qq);
+      qq = __dp4a(hi, hi, (unsigned)qq);
+      // -2q per byte as a signed byte: 0 - 2q never borrows across bytes
+      // when done as (0x80 - 2q) ^ 0x80 with 2q <= 30
+      m2q_lo[i] = (int)((0x80808080u - 2u * lo) ^ 0x80808080u);
+      m2q_hi[i] = (int)((0x80808080u - 2u * hi) ^ 0x80808080u);
     }
   }
   __device__ inline int dist(uint4 b) const {
-    uint32_t w[4] = {b.x, b.y, b.z, b.w};
-    int acc = 0;
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+    int acc = qq;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint32_t blo = w[i] & 0x0F0F0F0Fu, bhi = (w[i] >> 4) & 0x0F0F0F0Fu;
-      int dl = (int)((lo_or[i] - blo) ^ 0x80808080u);
-      int dh = (int)((hi_or[i] - bhi) ^ 0x80808080u);
-      acc = __dp4a(dl, dl, acc);
-      acc = __dp4a(dh, dh, acc);
+      const uint32_t blo = w[i] & 0x0F0F0F0Fu, bhi = (w[i] >> 4) & 0x0F0F0F0Fu;
+      acc = dp4a_us(blo, (int)blo, acc);
+      acc = dp4a_us(blo, m2q_lo[i], acc);
+      acc = dp4a_us(bhi, (int)bhi, acc);
+      acc = dp4a_us(bhi, m2q_hi[i], acc);
     }
     return acc;
   }
@@ -367,18 +437,18 @@ template <>
 struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
   uint32_t q[4];
   __device__ inline void load(const uint8_t* qcode, int chunk) {
-    uint4 v = *(const uint4*)(qcode + chunk * 16);
+    const uint4 v = *(const uint4*)(qcode + chunk * 16);
     q[0] = v.x;
     q[1] = v.y;
     q[2] = v.z;
     q[3] = v.w;
   }
   __device__ inline int dist(uint4 b) const {
-    uint32_t w[4] = {b.x, b.y, b.z, b.w};
+    const uint32_t w[4] = {b.x, b.y, b.z, b.w};
     unsigned acc = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint32_t d = __vabsdiffu4(q[i], w[i]);
+      const uint32_t d = __vabsdiffu4(q[i], w[i]);
       acc = __dp4a(d, d, acc);
     }
     return (int)acc;
@@ -389,7 +459,7 @@ struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
 // The search kernel.
 // ---------------------------------------------------------------------------
 template <int QUANT, int CPL, int PT>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const SearchArgs a) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -400,9 +470,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
   const uint32_t h_limit = (H >> 2) * 3;
   const uint32_t S = 1u << a.spill_bits;
   const uint32_t s_limit = (S >> 2) * 3;
+  float* stage = (float*)s.ht;
+  const uint32_t stage_rows_max = min(32u, (H * 4u) / (a.dim * 4u));
   constexpr int CPR = 32 / CPL;  // codes per gather round
   const int sub = lane & (CPL - 1);
   const int grp = lane / CPL;
+  auto vec_row = [&](uint32_t id) -> const float* { return a.vec + (size_t)id * a.dim; };
 
   while (true) {
     unsigned long long qi_ = 0;
@@ -410,9 +483,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
     const uint64_t qi = __shfl_sync(kFull, qi_, 0);
     if (qi >= a.nq) break;
 
-    // 1. query to shared memory
+    // 1. query -> shared memory (lane-major)
     const float* qg = a.queries + qi * a.dim;
-    for (uint32_t i = lane; i < a.dim_pad; i += 32) s.qf[i] = i < a.dim ? qg[i] : 0.0f;
+    for (uint32_t i = lane; i < a.dim_pad; i += 32) {
+      if (i < a.dim) s.qf[lane_major_pos(i, a.vec_c)] = qg[i];
+      else s.qf[i] = 0.0f;
+    }
     __syncwarp();
     int32_t status = 0;
 
@@ -422,7 +498,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
     uint32_t n_nav = 0;
     bool have_f32 = false;
     if (a.nav) {
-      if (!nav_descend(a, s, lane, &entry, &entry_f32, &n_nav)) status = 2;
+      if (!nav_descend(a, s, stage, stage_rows_max, lane, &entry, &entry_f32, &n_nav)) status = 2;
       have_f32 = true;
     }
     if (a.nav_only) {
@@ -432,6 +508,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
         if (a.n_nav) a.n_nav[qi] = n_nav;
         if (a.status) a.status[qi] = status;
       }
+      __syncwarp();
       continue;
     }
 
@@ -439,18 +516,18 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
     uint32_t ef = a.ef_fixed;
     if (a.adaptive) {
       if (!have_f32) {
-        float d2, dummy;
-        hw_l2_pair(s.qf, a.vec + (size_t)entry * a.dim, nullptr, a.dim, lane & 15, &d2, &dummy);
-        entry_f32 = d2;
+        if (lane == 0) s.cand_id[0] = entry;
+        __syncwarp();
+        rows_dist(s.qf, stage, stage_rows_max, s.cand_id, 1, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd, lane);
+        entry_f32 = s.nd[0];
         n_nav += 1;
       }
       uint32_t e;
       if (a.n_samples <= 1) {
         e = a.ef_mid;
       } else {
-        // rank = #samples < d (partition_point): the sorted samples are cut
-        // into 32 segments; the segment heads locate the answer, one segment
-        // is then counted.
+        // rank = #samples < d (partition_point): 32 segment heads locate the
+        // segment, which is then counted.
         const uint32_t ns = a.n_samples;
         const uint32_t seg = (ns + 31) / 32;
         const uint32_t head = (uint32_t)lane * seg;
@@ -476,19 +553,23 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
     uint32_t vcount = 0, expansions = 0;
     int sz = 0;
     if (status != 3) {
-      // encode the query
+      // encode the query (natural dims read through the lane-major map)
       if (QUANT == 0) {
         for (uint32_t b = lane; b < a.code_stride; b += 32) {
-          uint32_t d0 = 2 * b, d1 = 2 * b + 1;
-          uint32_t lo = d0 < a.dim ? quantize(s.qf[d0], a.q_inv[d0], a.q_neg[d0], a.levels) : 0u;
-          uint32_t hi = d1 < a.dim ? quantize(s.qf[d1], a.q_inv[d1], a.q_neg[d1], a.levels) : 0u;
+          const uint32_t d0 = 2 * b, d1 = 2 * b + 1;
+          const uint32_t lo =
+              d0 < a.dim ? quantize(s.qf[lane_major_pos(d0, a.vec_c)], a.q_inv[d0], a.q_neg[d0], a.levels) : 0u;
+          const uint32_t hi =
+              d1 < a.dim ? quantize(s.qf[lane_major_pos(d1, a.vec_c)], a.q_inv[d1], a.q_neg[d1], a.levels) : 0u;
           s.qcode[b] = (uint8_t)(lo | (hi << 4));
         }
       } else {
         for (uint32_t b = lane; b < a.code_stride; b += 32)
-          s.qcode[b] = b < a.dim ? (uint8_t)quantize(s.qf[b], a.q_inv[b], a.q_neg[b], a.levels) : (uint8_t)0;
+          s.qcode[b] = b < a.dim ? (uint8_t)quantize(s.qf[lane_major_pos(b, a.vec_c)], a.q_inv[b], a.q_neg[b],
+                                                     a.levels)
+                                 : (uint8_t)0;
       }
-      // clear the visited table
+      // clear the visited table (the staging rows of the descent are done)
       for (uint32_t i = lane * 4; i < H; i += 128) *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
       __syncwarp();
       QChunk<QUANT> qc;
@@ -497,18 +578,14 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
       bool spilled = false;
       uint32_t tcount = 0, scount = 0;
       // 4. entry
-      if (lane == 0) {
-        probe_insert<true>(s.ht, a.hash_bits, entry, true);
-        s.cand_id[0] = entry;
-      }
+      if (lane == 0) probe_insert<true>(s.ht, a.hash_bits, entry, true);
       tcount = 1;
       if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
       vcount = 1;
-      __syncwarp();
       {
         int pd = 0;
         if (grp == 0) {
-          uint4 v = __ldg((const uint4*)(a.codes + (size_t)entry * a.code_stride) + sub);
+          const uint4 v = __ldg((const uint4*)(a.codes + (size_t)entry * a.code_stride) + sub);
           pd = qc.dist(v);
         }
 #pragma unroll
@@ -531,18 +608,18 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
         if (lane == 0) s.pool_id[cursor] = node | kChecked;
         __syncwarp();
         ++expansions;
-        // neighbours (speculatively prefetched row of the next pool entry)
+        // neighbours (the row of the next pool entry is prefetched speculatively)
         uint32_t row[4];
-        const uint32_t* rg = a.adj + (size_t)node * a.r_pad + lane;
         if (node == pref_node) {
 #pragma unroll
           for (int r = 0; r < 4; ++r) row[r] = pref_row[r];
         } else {
+          const uint32_t* rg = a.adj + (size_t)node * a.r_pad + lane;
 #pragma unroll
           for (int r = 0; r < 4; ++r) row[r] = (uint32_t)r < RL ? __ldg(rg + 32 * r) : kSent;
         }
+        const int nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
         {
-          int nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
           if (nxt < sz) {
             pref_node = s.pool_id[nxt] & ~kChecked;
             const uint32_t* pg = a.adj + (size_t)pref_node * a.r_pad + lane;
@@ -554,130 +631,131 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
         }
         bool ended = false;  // first SENTINEL seen: degree reached
         bool overflow = false;
+        int first_insert = 0x7fffffff;
         for (uint32_t seg = 0; seg < RL && !ended; ++seg) {
-          uint32_t id = seg == 0 ? row[0] : seg == 1 ? row[1] : seg == 2 ? row[2] : row[3];
-          uint32_t sm = __ballot_sync(kFull, id == kSent);
-          int deg = sm ? __ffs(sm) - 1 : 32;
+          const uint32_t id = seg == 0 ? row[0] : seg == 1 ? row[1] : seg == 2 ? row[2] : row[3];
+          const uint32_t sm = __ballot_sync(kFull, id == kSent);
+          const int deg = sm ? __ffs(sm) - 1 : 32;
           if (sm) ended = true;
-          bool valid = lane < deg;
-          // duplicates inside the row: the first (lowest lane) occurrence counts
-          uint32_t peers = __match_any_sync(kFull, valid ? id : kSent);
-          bool leader = valid && (__ffs(peers) - 1 == lane);
+          if (deg == 0) continue;
+          // speculative gather: codes of every neighbour in the row are
+          // requested before the visited check, so the two latencies overlap
+          // (a neighbour that turns out visited costs one wasted 16 B load per lane)
+          uint4 data[CPL];
+#pragma unroll
+          for (int r = 0; r < CPL; ++r) {
+            const int idx = r * CPR + grp;
+            const uint32_t cid_raw = __shfl_sync(kFull, id, idx & 31);
+            const uint32_t cid = idx < deg ? cid_raw : 0u;  // address always in range
+            const uint4 v = __ldg((const uint4*)(a.codes + (size_t)cid * a.code_stride) + sub);
+            data[r] = idx < deg ? v : make_uint4(0, 0, 0, 0);
+          }
+          // rows hold no repeated id (the upload drops later repeats, which the
+          // reference treats as already visited), so every valid lane probes.
+          const bool valid = lane < deg;
           if (!spilled && tcount + 32 > h_limit) {
             if (spill == nullptr) {
               overflow = true;
               break;
             }
             // switch to the global spill table: clear it first
-            for (uint32_t i = lane * 4; i < S; i += 128) *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+            for (uint32_t i = lane * 4; i < S; i += 128)
+              *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
             __syncwarp();
             spilled = true;
           }
           bool is_new = false;
-          if (leader) {
+          if (valid) {
             if (!spilled) {
               is_new = probe_insert<true>(s.ht, a.hash_bits, id, true) == 1;
             } else {
-              int r = probe_insert<true>(s.ht, a.hash_bits, id, false);
+              const int r = probe_insert<true>(s.ht, a.hash_bits, id, false);
               if (r == 2) is_new = probe_insert<false>(spill, a.spill_bits, id, true) == 1;
             }
           }
-          uint32_t newm = __ballot_sync(kFull, is_new);
-          int nn = __popc(newm);
+          const uint32_t newm = __ballot_sync(kFull, is_new);
+          const int nn = __popc(newm);
           if (nn == 0) continue;
           if (!spilled) tcount += nn;
           else scount += nn;
-          int rank = __popc(newm & lanemask_lt(lane));
-          if (is_new) {
-            s.cand_id[rank] = id;
-            if (a.history && vcount + rank < a.hist_cap) a.history[qi * a.hist_cap + vcount + rank] = id;
+          if (a.history && is_new) {
+            const uint32_t pos = vcount + __popc(newm & lanemask_lt(lane));
+            if (pos < a.hist_cap) a.history[qi * a.hist_cap + pos] = id;
           }
           vcount += nn;
-          __syncwarp();
-          // gather codes of the new neighbours, integer distances
-          uint4 data[CPL];
+          // integer distances of the row (candidate idx -> cand_d[idx])
 #pragma unroll
           for (int r = 0; r < CPL; ++r) {
-            int idx = r * CPR + grp;
-            if (idx < nn) {
-              uint32_t cid = s.cand_id[idx];
-              data[r] = __ldg((const uint4*)(a.codes + (size_t)cid * a.code_stride) + sub);
-            } else {
-              data[r] = make_uint4(0, 0, 0, 0);
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < CPL; ++r) {
-            if (r * CPR < nn) {
+            if (r * CPR < deg) {
               int pdist = qc.dist(data[r]);
 #pragma unroll
               for (int o = 1; o < CPL; o <<= 1) pdist += __shfl_xor_sync(kFull, pdist, o);
-              int idx = r * CPR + grp;
-              if (sub == 0 && idx < nn) s.cand_d[idx] = (uint32_t)pdist;
+              const int idx = r * CPR + grp;
+              if (sub == 0 && idx < deg) s.cand_d[idx] = (uint32_t)pdist;
             }
           }
           __syncwarp();
-          const uint32_t my_d = lane < nn ? s.cand_d[lane] : 0xffffffffu;
-          const uint32_t my_id = lane < nn ? s.cand_id[lane] : kSent;
-          // merge into the pool (LinearPool::insert semantics, batched)
+          const uint32_t my_d = is_new ? s.cand_d[lane] : 0xffffffffu;
+          // merge the new neighbours (adjacency order) into the pool:
+          // LinearPool::insert semantics, batched
           const bool full = sz == (int)ef;
           const uint32_t worst = full ? s.pool_d[sz - 1] : 0xffffffffu;
-          const bool acc = lane < nn && (!full || my_d < worst);
+          const bool acc = is_new && (!full || my_d < worst);
           const uint32_t am = __ballot_sync(kFull, acc);
           const int na = __popc(am);
           __syncwarp();
           if (na > 0) {
-            uint32_t key = acc ? ((my_d << 5) | (uint32_t)lane) : 0xffffffffu;
-            key = bitonic32(key, lane);
-            const uint32_t cd = key >> 5;
-            const uint32_t cid = __shfl_sync(kFull, my_id, (int)(key & 31));
-            if (lane < na) s.cand_d[lane] = cd;
-            __syncwarp();
-            int cpos = 0, ub = 0;
-            if (lane < na) {
-              int lo = 0, hi = sz;  // # pool entries <= cd
+            // pool entries from the first insertion point onward move right
+            int cpos = 0x7fffffff;
+            if (acc) {
+              int lo = 0, hi = sz;  // # pool entries <= my_d (ties: pool first)
               while (lo < hi) {
-                int mid = (lo + hi) >> 1;
-                if (s.pool_d[mid] <= cd) lo = mid + 1;
+                const int mid = (lo + hi) >> 1;
+                if (s.pool_d[mid] <= my_d) lo = mid + 1;
                 else hi = mid;
               }
-              ub = lo;
-              cpos = lane + ub;
+              cpos = lo;
             }
-            const int start = __shfl_sync(kFull, ub, 0);
-            uint32_t rd[PT], ri[PT];
-            int rnp[PT];
+            const int start = (int)__reduce_min_sync(kFull, (unsigned)cpos);
+            uint32_t pd[PT], pi[PT];
+            int np[PT];
+            bool pv[PT];  // this lane's pool slot t holds an entry that may move
 #pragma unroll
             for (int t = 0; t < PT; ++t) {
-              int p = start + lane + 32 * t;
-              rnp[t] = 1 << 30;
-              if (p < sz) {
-                rd[t] = s.pool_d[p];
-                ri[t] = s.pool_id[p];
-                int lo = 0, hi = na;  // # candidates < pool distance
-                while (lo < hi) {
-                  int mid = (lo + hi) >> 1;
-                  if (s.cand_d[mid] < rd[t]) lo = mid + 1;
-                  else hi = mid;
-                }
-                rnp[t] = p + lo;
-              }
+              const int p = lane + 32 * t;
+              pv[t] = p >= start && p < sz;
+              pd[t] = pv[t] ? s.pool_d[p] : 0u;
+              pi[t] = pv[t] ? s.pool_id[p] : 0u;
+              np[t] = p;  // + (# accepted candidates closer), at most p + 32
             }
+            // one pass over the accepted candidates (adjacency order): rank
+            // among them by (distance, lane) and the shift of each pool entry
+            int crank = 0;
+            uint32_t m = am;
+            while (m) {
+              const int jl = __ffs(m) - 1;
+              m &= m - 1;
+              const uint32_t dj = __shfl_sync(kFull, my_d, jl);
+              crank += (dj < my_d) | ((dj == my_d) & (jl < lane));
+#pragma unroll
+              for (int t = 0; t < PT; ++t) np[t] += (int)(pv[t] && dj < pd[t]);
+            }
+            if (acc) cpos += crank;
             __syncwarp();
 #pragma unroll
             for (int t = 0; t < PT; ++t) {
-              if (rnp[t] < (int)ef) {
-                s.pool_d[rnp[t]] = rd[t];
-                s.pool_id[rnp[t]] = ri[t];
+              if (pv[t] && np[t] < (int)ef) {
+                s.pool_d[np[t]] = pd[t];
+                s.pool_id[np[t]] = pi[t];
               }
             }
-            if (lane < na && cpos < (int)ef) {
-              s.pool_d[cpos] = cd;
-              s.pool_id[cpos] = cid;
+            if (acc && cpos < (int)ef) {
+              s.pool_d[cpos] = my_d;
+              s.pool_id[cpos] = id;
             }
             __syncwarp();
             sz = min(sz + na, (int)ef);
-            if (start < cursor) cursor = start;
+            if (start < first_insert) first_insert = start;
           }
           if (spilled && scount > s_limit) {
             overflow = true;
@@ -688,7 +766,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
           status = 1;
           break;
         }
-        cursor = find_unchecked(s.pool_id, cursor, sz, lane);
+        // Entries before the popped one are expanded and `nxt` was the first
+        // unexpanded after it; an insert before `nxt` leaves it in place, so
+        // the next pop is the earlier of the two.
+        cursor = min(nxt, first_insert);
+        if (cursor > sz) cursor = sz;
       }
     }
 
@@ -696,34 +778,43 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) search_kernel(const Searc
     const uint64_t krr = (uint64_t)a.k * (uint64_t)max(a.rr, 1u);
     const uint64_t krr_k = krr > (uint64_t)a.k ? krr : (uint64_t)a.k;
     const int rn = (int)(krr_k < (uint64_t)sz ? krr_k : (uint64_t)sz);
-    float* rdist = (float*)s.ht;
-    {
-      const int h = lane >> 4, j = lane & 15;
-      for (int e0 = 0; e0 < rn; e0 += 4) {
-        int ea = e0 + h, eb = e0 + 2 + h;
-        const float* ra = ea < rn ? a.vec + (size_t)(s.pool_id[ea] & ~kChecked) * a.dim : nullptr;
-        const float* rb = eb < rn ? a.vec + (size_t)(s.pool_id[eb] & ~kChecked) * a.dim : nullptr;
-        float da, db;
-        hw_l2_pair(s.qf, ra, rb, a.dim, j, &da, &db);
-        if (j == 0) {
-          if (ea < rn) rdist[ea] = da;
-          if (eb < rn) rdist[eb] = db;
-        }
-      }
+    float* rdist = (float*)s.pool_d;  // pool distances are no longer needed
+    for (int c0 = 0; c0 < rn; c0 += 32) {
+      const int cn = min(32, rn - c0);
+      if (lane < cn) s.cand_id[lane] = s.pool_id[c0 + lane] & ~kChecked;
+      __syncwarp();
+      rows_dist(s.qf, stage, stage_rows_max, s.cand_id, cn, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd, lane);
+      if (lane < cn) rdist[c0 + lane] = s.nd[lane];
+      __syncwarp();
     }
-    __syncwarp();
     const int kout = min((int)a.k, rn);
-    // stable ascending order by (total_cmp(dist), pool position)
-    for (int i = lane; i < rn; i += 32) {
-      const uint32_t ki = total_order_key(rdist[i]);
-      int rank = 0;
-      for (int jj = 0; jj < rn; ++jj) {
-        const uint32_t kj = total_order_key(rdist[jj]);
-        rank += (kj < ki) || (kj == ki && jj < i);
-      }
-      if (rank < kout) {
-        a.ids[qi * a.k + rank] = s.pool_id[i] & ~kChecked;
-        if (a.dists) a.dists[qi * a.k + rank] = rdist[i];
+    // k smallest by (total_cmp(dist), pool position): repeated warp minimum;
+    // each lane owns positions lane, lane+32, ...
+    {
+      uint32_t taken = 0;  // bit t: position lane+32t already output
+      for (int r = 0; r < kout; ++r) {
+        uint32_t best = 0xffffffffu;
+        int bt = -1;
+        for (int t = 0; lane + 32 * t < rn; ++t) {
+          if (taken & (1u << t)) continue;
+          const uint32_t kk = total_order_key(rdist[lane + 32 * t]);
+          if (bt < 0 || kk < best) {  // strict: the lowest position wins a tie within a lane
+            best = kk;
+            bt = t;
+          }
+        }
+        const uint32_t m = __reduce_min_sync(kFull, best);
+        // ties across lanes: the smallest position, i.e. lowest t, then lowest lane
+        const int myt = (best == m && bt >= 0) ? bt : 0x7fff;
+        const int mt = (int)__reduce_min_sync(kFull, (unsigned)myt);
+        const uint32_t who = __ballot_sync(kFull, best == m && bt == mt);
+        const int wl = __ffs(who) - 1;
+        if (lane == wl) {
+          const int i = lane + 32 * bt;
+          taken |= 1u << bt;
+          a.ids[qi * a.k + r] = s.pool_id[i] & ~kChecked;
+          if (a.dists) a.dists[qi * a.k + r] = rdist[i];
+        }
       }
     }
     for (int r = kout + lane; r < (int)a.k; r += 32) {
