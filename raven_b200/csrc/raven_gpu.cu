@@ -51,7 +51,7 @@ struct raven_index {
   float* d_samples = nullptr;
   // launch tuning
   int hash_bits_override = 0;
-  int spill_bits = 14;
+  int spill_bits_override = 0;
 };
 
 namespace {
@@ -380,7 +380,7 @@ std::vector<uint32_t> ef_table(uint32_t S, uint32_t min_ef, uint32_t max_ef, flo
 }
 
 struct Plan {
-  int quant, cpl, pt, hash_bits;
+  int quant, cpl, pt, hash_bits, spill_bits;
   uint32_t ef_cap;
   uint32_t smem_warp, smem_block;
   std::vector<uint32_t> table;
@@ -417,11 +417,16 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   pl->pt = ef_cap <= 64 ? 2 : ef_cap <= 128 ? 4 : 8;
   uint32_t hb = ix->hash_bits_override;
   if (hb == 0) {
-    // 4096 slots (16 KB per warp): past 3/4 load a query continues in its
-    // global spill table, which measured cheaper than the lower residency of
-    // larger shared tables on 1M-node graphs at ef 50..140
-    hb = ef_cap <= 32 ? 11 : 12;
+    // Shared-memory visited slots per warp. Past 3/4 load a query continues
+    // in its global (L2-resident) spill table, whose probes overlap the code
+    // gather; a smaller shared table buys residency. Measured on a 1M-node
+    // graph: 2048 slots best at ef <= 64, 1024 beyond.
+    hb = ef_cap <= 64 ? 11 : 10;
   }
+  // spill level A ~32 visits per unit of ef; level B (8x) catches outliers
+  uint32_t sb = ix->spill_bits_override;
+  if (sb == 0) sb = ef_cap <= 64 ? 12 : ef_cap <= 160 ? 13 : 14;
+  pl->spill_bits = (int)sb;
   // the visited table doubles as the row staging area: it must hold a row
   while ((1u << hb) < ix->dim_pad) ++hb;
   pl->hash_bits = (int)hb;
@@ -454,7 +459,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   int grid = (int)std::max<uint64_t>(1, std::min(grid64, need));
   const uint64_t slots = (uint64_t)grid * kWarpsPerBlock;
   // per-call scratch: work counter, spill tables, ef table (stream ordered)
-  const size_t spill_bytes = (size_t)slots << ix->spill_bits << 2;
+  const size_t spill_bytes = (size_t)slots * (9ull << pl.spill_bits) * 4;  // levels A + B per slot
   const size_t table_bytes = pl.table.size() * 4;
   size_t total = 256 + spill_bytes + ((table_bytes + 255) & ~(size_t)255);
   uint8_t* scratch = nullptr;
@@ -509,8 +514,9 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.k = p->k;
   a.rr = std::max<uint32_t>(p->rerank_factor, 1);
   a.hash_bits = pl.hash_bits;
-  a.spill_bits = ix->spill_bits;
+  a.spill_bits = pl.spill_bits;
   a.spill = spill;
+  a.n_slots = slots;
   a.smem_per_warp = pl.smem_warp;
   a.queries = d_q;
   a.nq = nq;
@@ -989,7 +995,7 @@ int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bit
   if (hash_bits && (hash_bits < 8 || hash_bits > 14)) return fail(RAVEN_EINVAL, "hash_bits must be in 8..14");
   if (spill_bits && (spill_bits < 10 || spill_bits > 20)) return fail(RAVEN_EINVAL, "spill_bits must be in 10..20");
   ix->hash_bits_override = hash_bits;
-  if (spill_bits) ix->spill_bits = spill_bits;
+  ix->spill_bits_override = spill_bits;
   return RAVEN_OK;
 }
 

@@ -34,7 +34,7 @@ constexpr uint32_t kChecked = 0x80000000u;
 constexpr uint32_t kGidBit = 0x80000000u;  // nav handle: global id (node without upper list)
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr int kWarpsPerBlock = 4;
-constexpr int kMinBlocksPerSm = 4;  // shared memory, not registers, bounds residency
+constexpr int kMinBlocksPerSm = 6;  // 80 registers/thread: the measured best residency trade-off
 constexpr uint32_t kNavStepLimit = 1u << 16;
 
 struct SearchArgs {
@@ -68,8 +68,9 @@ struct SearchArgs {
   uint32_t ef_fixed, k, rr;
   uint32_t dist_bits;   // bits of the largest possible quantised distance
   uint32_t hash_bits;   // shared-memory visited table: 1 << hash_bits slots
-  uint32_t spill_bits;  // global spill table per warp slot: 1 << spill_bits slots
-  uint32_t* spill;
+  uint32_t spill_bits;  // global spill tables per warp slot: level A 1 << spill_bits slots
+  uint32_t* spill;      // (all slots' A tables contiguous), then level B tables 8x larger
+  uint64_t n_slots;     // warp slots of the launch (A region = n_slots << spill_bits)
   uint32_t smem_per_warp;
   // queries (natural layout)
   const float* __restrict__ queries;
@@ -378,6 +379,13 @@ __device__ inline int probe_insert(uint32_t* t, uint32_t bits, uint32_t id, bool
   return insert ? 3 : 2;  // table full (not reached: load is capped at 3/4)
 }
 
+// Level B of the visited set (outlier queries only): look up level A, then
+// insert into B. Out of line to keep the common path compact.
+__device__ __noinline__ bool probe_level_b(uint32_t* spill_a, uint32_t* spill_b, uint32_t bits_a, uint32_t id) {
+  if (probe_insert<false>(spill_a, bits_a, id, false) != 2) return false;
+  return probe_insert<false>(spill_b, bits_a + 3, id, true) == 1;
+}
+
 __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, int lane) {
   for (int base = from & ~31; base < sz; base += 32) {
     const int p = base + lane;
@@ -465,11 +473,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
   const int wib = threadIdx.x >> 5;
   const WarpSmem s = carve(smem_raw + (size_t)wib * a.smem_per_warp, a, PT);
   const uint32_t slot = blockIdx.x * kWarpsPerBlock + wib;
+  // level A tables are contiguous (hot, L2/TLB friendly); level B only for outliers
   uint32_t* spill = a.spill ? a.spill + ((size_t)slot << a.spill_bits) : nullptr;
+  uint32_t* spill_b = a.spill ? a.spill + (a.n_slots << a.spill_bits) + ((size_t)slot << (a.spill_bits + 3)) : nullptr;
+  const uint32_t spill_b_bits = a.spill_bits + 3;
   const uint32_t H = 1u << a.hash_bits;
   const uint32_t h_limit = (H >> 2) * 3;
   const uint32_t S = 1u << a.spill_bits;
   const uint32_t s_limit = (S >> 2) * 3;
+  const uint32_t SB = S << 3;
+  const uint32_t sb_limit = (SB >> 2) * 3;
   float* stage = (float*)s.ht;
   const uint32_t stage_rows_max = min(32u, (H * 4u) / (a.dim * 4u));
   constexpr int CPR = 32 / CPL;  // codes per gather round
@@ -575,7 +588,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       QChunk<QUANT> qc;
       qc.load(s.qcode, sub);
 
-      bool spilled = false;
+      int level = 0;
       uint32_t tcount = 0, scount = 0;
       // 4. entry
       if (lane == 0) probe_insert<true>(s.ht, a.hash_bits, entry, true);
@@ -653,30 +666,40 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
           // rows hold no repeated id (the upload drops later repeats, which the
           // reference treats as already visited), so every valid lane probes.
           const bool valid = lane < deg;
-          if (!spilled && tcount + 32 > h_limit) {
+          // visited-set level: 0 shared table, 1 spill A, 2 spill B
+          if (level == 0 && tcount + 32 > h_limit) {
             if (spill == nullptr) {
               overflow = true;
               break;
             }
-            // switch to the global spill table: clear it first
             for (uint32_t i = lane * 4; i < S; i += 128)
               *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
             __syncwarp();
-            spilled = true;
+            level = 1;
+          } else if (level == 1 && scount + 32 > s_limit) {
+            for (uint32_t i = lane * 4; i < SB; i += 128)
+              *(uint4*)(spill_b + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+            __syncwarp();
+            level = 2;
+            scount = 0;
+          } else if (level == 2 && scount + 32 > sb_limit) {
+            overflow = true;
+            break;
           }
           bool is_new = false;
           if (valid) {
-            if (!spilled) {
+            // every id lives in exactly one level; insert into the current one
+            if (level == 0) {
               is_new = probe_insert<true>(s.ht, a.hash_bits, id, true) == 1;
-            } else {
-              const int r = probe_insert<true>(s.ht, a.hash_bits, id, false);
-              if (r == 2) is_new = probe_insert<false>(spill, a.spill_bits, id, true) == 1;
+            } else if (probe_insert<true>(s.ht, a.hash_bits, id, false) == 2) {
+              if (level == 1) is_new = probe_insert<false>(spill, a.spill_bits, id, true) == 1;
+              else is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
             }
           }
           const uint32_t newm = __ballot_sync(kFull, is_new);
           const int nn = __popc(newm);
           if (nn == 0) continue;
-          if (!spilled) tcount += nn;
+          if (level == 0) tcount += nn;
           else scount += nn;
           if (a.history && is_new) {
             const uint32_t pos = vcount + __popc(newm & lanemask_lt(lane));
@@ -757,10 +780,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
             sz = min(sz + na, (int)ef);
             if (start < first_insert) first_insert = start;
           }
-          if (spilled && scount > s_limit) {
-            overflow = true;
-            break;
-          }
+
         }
         if (overflow) {
           status = 1;

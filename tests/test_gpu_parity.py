@@ -273,17 +273,21 @@ def test_quantiser_not_uploaded_is_state_error(small_case, raven_lib):
     assert e.value.code == L.RAVEN_ESTATE
 
 
-def test_small_visited_table_spills_exactly(small):
-    """Force the shared-memory visited table to overflow into the global spill
-    table; results stay exact."""
+@pytest.mark.parametrize("hash_bits,spill_bits,ef", [(8, 0, 100), (8, 10, 200)])
+def test_small_visited_table_spills_exactly(small, hash_bits, spill_bits, ef):
+    """Force the shared-memory visited table over into the global spill levels
+    (256 shared slots; with 1024-slot level A, level B takes the rest); results
+    stay exact."""
     base, q, g, dev, oi = small
-    dev.set_tuning(hash_bits=8)  # 256 slots: spills after ~192 visits
+    dev.set_tuning(hash_bits=hash_bits, spill_bits=spill_bits)
     try:
-        got = dev.search(q, _params(ef=100), history_cap=4096)
-        exp = oi.search(q, k=10, ef=100, rerank_factor=8, history_cap=4096)
+        got = dev.search(q, _params(ef=ef), history_cap=8192)
+        exp = oi.search(q, k=10, ef=ef, rerank_factor=8, history_cap=8192)
         _compare(got, exp)
+        if spill_bits:
+            assert got["visited"].max() > 192 + 768  # some queries reached level B
     finally:
-        dev.set_tuning(hash_bits=0)
+        dev.set_tuning(hash_bits=0, spill_bits=0)
 
 
 def test_device_entry_point_matches_host_entry(small):
@@ -370,3 +374,26 @@ def test_gmm100k_full_parity(oracle, raven_lib):
     gi, _ = oracle.bruteforce(base, q[:1000], 10)
     rec = np.mean([len(set(got["ids"][j]) & set(gi[j])) / 10 for j in range(1000)])
     assert rec >= 0.95
+
+
+def test_gmm1m_headline_parity(oracle, raven_lib):
+    """The headline 1M x 128 workload (SQ4, k=10, rr=8) at ef=50 and at its
+    recall>=0.95 operating point ef=140: 2,000 queries compared with the oracle
+    on every output, and no query of a 10,000 batch hits a capacity limit."""
+    from raven_b200 import datasets
+    from raven_b200.index import DeviceIndex
+
+    wl = "gmm1m-d128-sparse"
+    if not os.path.exists(datasets.index_path(wl)):
+        pytest.skip("cached 1M index file not present (build it with raven_b200.datasets.load_or_build)")
+    base, _ = datasets.make(wl, nq=1)
+    q = datasets.make_queries(wl, 10000)
+    g = datasets.load_or_build(wl, base=base)
+    dev = DeviceIndex(g, base, sq4=True)
+    oi = _oracle_for(oracle, g, base, sq8=False, adaptive=False)
+    for ef in (50, 140):
+        full = dev.search(q, _params(ef=ef))
+        assert np.all(full["status"] == 0)
+        got = dev.search(q[:2000], _params(ef=ef), history_cap=8192)
+        exp = oi.search(q[:2000], k=10, ef=ef, rerank_factor=8, history_cap=8192)
+        _compare(got, exp)
