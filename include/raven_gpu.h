@@ -160,6 +160,25 @@ RAVEN_API int raven_search_batch(raven_index* ix, const float* queries, uint64_t
 RAVEN_API int raven_search_batch_device(raven_index* ix, const float* d_queries, uint64_t nq, const raven_search_params* p,
                               const raven_search_outputs* d_out, void* stream);
 
+/* Device-buffer search that allocates nothing (no counterpart in the
+ * reference). For callers that cannot allocate device memory while serving —
+ * e.g. when another allocator has reserved the GPU's memory up front, or a hard
+ * memory budget must be fixed at start-up — the per-call scratch (work counter,
+ * AdaptiveEf table, visited-set spill tables) comes from one fixed 64 MiB
+ * device array that every GPU loading this library holds until the process
+ * exits, instead of the stream-ordered pool used by raven_search_batch_device.
+ * Same inputs, outputs and results. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * (e.g. on two streams) race and must be serialised by the caller. To fit the
+ * array, spill tables are smaller (each query can still hold over 14,000 visited
+ * nodes before reporting RAVEN_Q_VISITED_OVERFLOW) and fewer warps may be
+ * resident. Returns RAVEN_ELIMIT if a call cannot fit (an AdaptiveEf table of
+ * more than 4032 samples). */
+RAVEN_API int raven_search_batch_device_noalloc(raven_index* ix, const float* d_queries, uint64_t nq,
+                                                const raven_search_params* p, const raven_search_outputs* d_out,
+                                                void* stream);
+
 /* Exact k-nearest neighbours over the uploaded f32 vectors (recall ground
  * truth; no reference counterpart — the reference reads SIFT groundtruth
  * files, src/bin/sq4_ef_sweep.rs:61). Device buffers; ties broken by id. */

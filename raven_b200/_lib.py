@@ -124,6 +124,8 @@ SIGNATURES = {
                                      C.POINTER(SearchOutputs), C.c_void_p]),
     "raven_search_batch_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.POINTER(SearchParams),
                                             C.POINTER(SearchOutputs), C.c_void_p]),
+    "raven_search_batch_device_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.POINTER(SearchParams),
+                                                    C.POINTER(SearchOutputs), C.c_void_p]),
     "raven_knn_exact_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint32, C.c_void_p, C.c_void_p,
                                          C.c_void_p]),
     "raven_merge_topk_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint64, C.c_uint32,

@@ -1000,3 +1000,149 @@ int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bit
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Search without allocation: scratch from a fixed device array.
+//
+// Some callers cannot allocate device memory at search time: a serving loop
+// whose GPU memory is entirely reserved up front by another allocator (a
+// framework's caching pool), a process that has to keep a hard memory budget
+// and fail at start-up rather than mid-request, or code that must not make the
+// allocator calls that can synchronise the device. For them this entry point
+// takes the per-call scratch (work counter, AdaptiveEf table, visited-set spill
+// tables) from g_noalloc_scratch, a file-scope device array of
+// kNoAllocScratchBytes that every GPU which loads this library holds until the
+// process exits. The caller still provides queries and outputs.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB per GPU
+constexpr size_t kNoAllocHeader = 16384;               // counter + ef table (<= 2001 u32)
+constexpr uint32_t kNoAllocMaxSpillBits = 11;          // spill level A 8 KB, level B 64 KB per warp
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+uint8_t* g_noalloc_ptr[256] = {};  // device address of g_noalloc_scratch, per device ordinal
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device memory:
+// the device address comes from cudaGetSymbolAddress, once per device, with
+// that device current.
+int noalloc_scratch(int device, uint8_t** out) {
+  if (device < 0 || device >= 256) return fail(RAVEN_EINVAL, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(RAVEN_ECUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    g_noalloc_ptr[device] = (uint8_t*)ptr;
+  }
+  *out = g_noalloc_ptr[device];
+  return RAVEN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
+                                      const raven_search_outputs* o, void* stream) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  if (nq && !d_q) return fail(RAVEN_EINVAL, "null queries");
+  Plan pl;
+  int rc = make_plan(ix, p, &pl);
+  if (rc) return rc;
+  if (nq == 0) return RAVEN_OK;
+  if (!o || !o->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
+  if (pl.table.size() * 4 + 256 > kNoAllocHeader)
+    return fail(RAVEN_ELIMIT, "AdaptiveEf table larger than the fixed scratch header (max 4032 samples)");
+  CU(cudaSetDevice(ix->device));
+  uint8_t* scratch = nullptr;
+  if ((rc = noalloc_scratch(ix->device, &scratch))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
+  // spill tables sized to fit the fixed array: smaller level A, and as many
+  // resident warps as the remaining bytes allow
+  const uint32_t sb = std::min<uint32_t>((uint32_t)pl.spill_bits, kNoAllocMaxSpillBits);
+  const size_t per_slot = (9ull << sb) * 4;
+  const uint64_t max_slots = (kNoAllocScratchBytes - kNoAllocHeader) / per_slot;
+  int blocks_per_sm = 0;
+  CU(dispatch(pl.quant, pl.cpl, pl.pt, true, SearchArgs{}, pl.smem_block, 0, st, &blocks_per_sm));
+  if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
+  const uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const uint64_t grid64 = std::min<uint64_t>({(uint64_t)blocks_per_sm * ix->num_sms, need, max_slots / kWarpsPerBlock});
+  if (grid64 == 0) return fail(RAVEN_ELIMIT, "fixed scratch array too small for one block of spill tables");
+  const int grid = (int)grid64;
+  const uint64_t slots = (uint64_t)grid * kWarpsPerBlock;
+  unsigned long long* counter = (unsigned long long*)scratch;
+  uint32_t* table = (uint32_t*)(scratch + 256);
+  uint32_t* spill = (uint32_t*)(scratch + kNoAllocHeader);
+  // the array keeps the previous call's contents: the work counter must start
+  // at zero; spill tables are cleared by each query on first use
+  CU(cudaMemsetAsync(counter, 0, 8, st));
+  if (!pl.table.empty())
+    CU(cudaMemcpyAsync(table, pl.table.data(), pl.table.size() * 4, cudaMemcpyHostToDevice, st));
+  SearchArgs a{};
+  a.vec = ix->d_vec;
+  a.dim = ix->dim;
+  a.dim_pad = ix->dim_pad;
+  a.vec_c = ix->dim / 16;
+  a.vec_rem = ix->dim % 16;
+  a.adj = ix->d_adj;
+  a.r_pad = ix->r_pad;
+  a.codes = ix->d_codes[pl.quant];
+  a.code_stride = ix->q_stride[pl.quant];
+  a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
+  a.q_neg = ix->d_qparams[pl.quant] + 4 * ix->dim;
+  a.levels = pl.quant == 0 ? 15.0f : 255.0f;
+  {
+    const uint64_t per_dim = pl.quant == 0 ? 225ull : 65025ull;
+    const uint64_t dims = pl.quant == 0 ? (uint64_t)ix->q_stride[0] * 2 : (uint64_t)ix->q_stride[1];
+    const uint64_t mx = per_dim * dims;
+    uint32_t b = 0;
+    while (b < 32 && (mx >> b) != 0) ++b;
+    a.dist_bits = b;
+  }
+  a.entry = ix->entry;
+  a.nav = ix->has_nav ? 1 : 0;
+  a.nav_entry_h = ix->nav_entry_h;
+  a.nav_max_level = ix->nav_max_level;
+  a.nav_k = ix->nav_k;
+  a.nav_stride_levels = ix->nav_stride_levels;
+  a.nav_vec = ix->d_nav_vec;
+  a.nav_e = ix->d_nav_e;
+  a.nav_gid = ix->d_nav_gid;
+  a.adaptive = p->adaptive ? 1 : 0;
+  a.samples = ix->d_samples;
+  a.n_samples = (uint32_t)ix->h_samples.size();
+  a.ef_table = table;
+  a.ef_mid = pl.ef_mid;
+  a.ef_fixed = p->ef;
+  a.k = p->k;
+  a.rr = std::max<uint32_t>(p->rerank_factor, 1);
+  a.hash_bits = pl.hash_bits;
+  a.spill_bits = sb;
+  a.spill = spill;
+  a.n_slots = slots;
+  a.smem_per_warp = pl.smem_warp;
+  a.queries = d_q;
+  a.nq = nq;
+  a.ids = o->ids;
+  a.dists = o->dists;
+  a.counts = o->counts;
+  a.visited = o->visited;
+  a.ef_used = o->ef_used;
+  a.status = o->status;
+  a.n_nav = o->n_nav;
+  a.expansions = o->expansions;
+  a.history = o->history;
+  a.hist_cap = o->history ? o->history_cap : 0;
+  a.hist_len = o->history_len;
+  a.counter = counter;
+  a.nav_only = 0;
+  const cudaError_t e = dispatch(pl.quant, pl.cpl, pl.pt, false, a, pl.smem_block, grid, st, nullptr);
+  if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
+  return RAVEN_OK;
+}
+
+}  // extern "C"
