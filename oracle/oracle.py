@@ -299,3 +299,26 @@ def bruteforce(base, queries, k=10, threads=0):
     lib().oracle_bruteforce(_p(b, C.c_float), b.shape[0], _p(q, C.c_float), q.shape[0], b.shape[1], k, threads,
                             _p(ids, C.c_uint32), _p(ds, C.c_float))
     return ids, ds
+
+
+def merge_shard_lists(ids, dists, counts, shard_size, k):
+    """Host merge of per-shard top-k lists (shard-major [S][nq][k], ids local
+    to each shard) into global top-k per query, the rule a host-side combiner
+    of per-shard reference searches follows: sort the valid entries by
+    (distance, shard, rank in the shard's list), keep k; global id =
+    shard * shard_size + local id. Missing entries are 0 / 0.0."""
+    ids = np.asarray(ids, np.uint32)
+    dists = np.asarray(dists, np.float32)
+    counts = np.asarray(counts, np.int64)
+    S, nq, kk = ids.shape
+    out_i = np.zeros((nq, k), np.uint32)
+    out_d = np.zeros((nq, k), np.float32)
+    out_c = np.zeros(nq, np.uint32)
+    for qi in range(nq):
+        c = [(float(dists[s, qi, r]), s, r) for s in range(S) for r in range(min(int(counts[s, qi]), kk))]
+        c.sort()
+        for r, (d, s, rr) in enumerate(c[:k]):
+            out_d[qi, r] = d
+            out_i[qi, r] = s * shard_size + int(ids[s, qi, rr])
+        out_c[qi] = min(len(c), k)
+    return out_i, out_d, out_c

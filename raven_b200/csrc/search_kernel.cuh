@@ -386,6 +386,52 @@ __device__ __noinline__ bool probe_level_b(uint32_t* spill_a, uint32_t* spill_b,
   return probe_insert<false>(spill_b, bits_a + 3, id, true) == 1;
 }
 
+// Level A of the visited set, warp-cooperative. The table belongs to this
+// warp alone and the lanes' ids are distinct, so insertion needs no atomics:
+// each lane looks for its id in the bucket `v` it has already read (bucket `b`,
+// read early so that the read overlaps the code gather), then claims the first
+// empty slot it sees; lanes claiming the same slot are settled by
+// __match_any_sync (lowest lane wins, the others see the slot taken and try
+// again), and a lane whose bucket is full reads the next one. Stores are plain
+// and need no reply. Returns true for a first visit. Linear probing over
+// 4-slot buckets with no deletions, so "absent" = an empty slot was reached.
+// The loop ends: every round either places one lane per contended slot or
+// moves every unplaced lane to its next bucket, and the load is capped at 3/4.
+__device__ inline bool spill_insert_warp(uint32_t* t, uint32_t bits, uint32_t id, bool need, uint32_t b, uint4 v,
+                                         int lane) {
+  constexpr uint32_t kTaken = 0xFFFFFFFEu;  // slot claimed this round by another lane (never an id)
+  const uint32_t bmask = (1u << (bits - 2)) - 1u;
+  bool pending = need, is_new = false;
+  for (uint32_t round = 0; round <= bmask + 33u; ++round) {
+    int e = -1;
+    if (pending) {
+      if (v.x == id || v.y == id || v.z == id || v.w == id) pending = false;
+      else e = v.x == kEmpty ? 0 : v.y == kEmpty ? 1 : v.z == kEmpty ? 2 : v.w == kEmpty ? 3 : -1;
+    }
+    const bool want = pending && e >= 0;
+    const uint32_t wm = __ballot_sync(kFull, want);
+    if (want) {
+      const uint32_t key = 4u * b + (uint32_t)e;
+      const uint32_t same = __match_any_sync(wm, key);
+      if (__ffs(same) - 1 == lane) {
+        t[key] = id;
+        pending = false;
+        is_new = true;
+      } else if (e == 0) v.x = kTaken;
+      else if (e == 1) v.y = kTaken;
+      else if (e == 2) v.z = kTaken;
+      else v.w = kTaken;
+    }
+    __syncwarp();  // this round's stores are visible to the lanes that read next
+    if (pending && e < 0) {
+      b = (b + 1) & bmask;
+      v = __ldcv((const uint4*)(t + 4 * b));
+    }
+    if (!__any_sync(kFull, pending)) break;
+  }
+  return is_new;
+}
+
 __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, int lane) {
   for (int base = from & ~31; base < sz; base += 32) {
     const int p = base + lane;
@@ -476,7 +522,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
   // level A tables are contiguous (hot, L2/TLB friendly); level B only for outliers
   uint32_t* spill = a.spill ? a.spill + ((size_t)slot << a.spill_bits) : nullptr;
   uint32_t* spill_b = a.spill ? a.spill + (a.n_slots << a.spill_bits) + ((size_t)slot << (a.spill_bits + 3)) : nullptr;
-  const uint32_t spill_b_bits = a.spill_bits + 3;
   const uint32_t H = 1u << a.hash_bits;
   const uint32_t h_limit = (H >> 2) * 3;
   const uint32_t S = 1u << a.spill_bits;
@@ -660,8 +705,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
             const int idx = r * CPR + grp;
             const uint32_t cid_raw = __shfl_sync(kFull, id, idx & 31);
             const uint32_t cid = idx < deg ? cid_raw : 0u;  // address always in range
-            const uint4 v = __ldg((const uint4*)(a.codes + (size_t)cid * a.code_stride) + sub);
-            data[r] = idx < deg ? v : make_uint4(0, 0, 0, 0);
+            // lanes past the degree load node 0's codes; their distances are never stored
+            data[r] = __ldg((const uint4*)(a.codes + (size_t)cid * a.code_stride) + sub);
           }
           // rows hold no repeated id (the upload drops later repeats, which the
           // reference treats as already visited), so every valid lane probes.
@@ -687,14 +732,18 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
             break;
           }
           bool is_new = false;
-          if (valid) {
-            // every id lives in exactly one level; insert into the current one
-            if (level == 0) {
-              is_new = probe_insert<true>(s.ht, a.hash_bits, id, true) == 1;
-            } else if (probe_insert<true>(s.ht, a.hash_bits, id, false) == 2) {
-              if (level == 1) is_new = probe_insert<false>(spill, a.spill_bits, id, true) == 1;
-              else is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
-            }
+          // every id lives in exactly one level; insert into the current one
+          if (level == 0) {
+            if (valid) is_new = probe_insert<true>(s.ht, a.hash_bits, id, true) == 1;
+          } else if (level == 1) {
+            // home bucket of level A read before the shared lookup: the two overlap
+            const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
+            uint4 sv = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+            if (valid) sv = __ldcv((const uint4*)(spill + 4 * sbk));
+            const bool need = valid && probe_insert<true>(s.ht, a.hash_bits, id, false) == 2;
+            is_new = spill_insert_warp(spill, a.spill_bits, id, need, sbk, sv, lane);
+          } else if (valid && probe_insert<true>(s.ht, a.hash_bits, id, false) == 2) {
+            is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
           }
           const uint32_t newm = __ballot_sync(kFull, is_new);
           const int nn = __popc(newm);
