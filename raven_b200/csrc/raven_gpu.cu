@@ -430,7 +430,7 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   // the visited table doubles as the row staging area: it must hold a row
   while ((1u << hb) < ix->dim_pad) ++hb;
   pl->hash_bits = (int)hb;
-  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pt, hb);
+  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pt, hb, ix->r_pad);
   pl->smem_block = pl->smem_warp * kWarpsPerBlock;
   return RAVEN_OK;
 }

@@ -100,14 +100,15 @@ struct WarpSmem {
   uint32_t* cand_id;  // 32
   uint32_t* cand_d;   // 32
   float* nd;          // 32
+  uint32_t* rowbuf;   // 2 x r_pad: adjacency rows prefetched by cp.async
   uint32_t* ht;       // 1 << hash_bits; also the row staging area outside the beam search
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
 __host__ __device__ inline uint32_t warp_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pt,
-                                                    uint32_t hash_bits) {
-  return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(32 * pt * 4) + 3 * 128 +
+                                                    uint32_t hash_bits, uint32_t r_pad) {
+  return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(32 * pt * 4) + 3 * 128 + 2 * r_pad * 4 +
          align16((1u << hash_bits) * 4);
 }
 
@@ -128,6 +129,8 @@ __device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, int pt) {
   o += 128;
   s.nd = (float*)(base + o);
   o += 128;
+  s.rowbuf = (uint32_t*)(base + o);
+  o += 2 * a.r_pad * 4;
   s.ht = (uint32_t*)(base + o);
   return s;
 }
@@ -151,6 +154,12 @@ __device__ inline void cp_async16(void* smem, const void* gmem) {
 __device__ inline void cp_async4(void* smem, const void* gmem) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+// Asynchronous copy of node's adjacency row (r_pad ids, 16 B per lane) into
+// `buf`, as its own commit group.
+__device__ inline void prefetch_row(const uint32_t* adj, uint32_t r_pad, uint32_t* buf, uint32_t node, int lane) {
+  if ((uint32_t)lane < (r_pad >> 2)) cp_async16(buf + 4 * lane, adj + (size_t)node * r_pad + 4 * lane);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 __device__ inline void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
@@ -379,6 +388,42 @@ __device__ inline int probe_insert(uint32_t* t, uint32_t bits, uint32_t id, bool
   return insert ? 3 : 2;  // table full (not reached: load is capped at 3/4)
 }
 
+// Level 0 of the visited set: a two-choice bucketed table in shared memory.
+// An id lives in bucket h1(id) or h2(id) (4 slots each), so a lookup is two
+// independent 16-byte reads and never a probe chain, and inserts fill the
+// emptier bucket, which keeps the buckets even up to high load.
+__device__ inline uint32_t hash2_slot(uint32_t id, uint32_t bits) {
+  return ((id ^ (id >> 15)) * 0x2C1B3C6Du) >> (32 - bits);
+}
+__device__ inline bool bucket_has(uint4 v, uint32_t id) { return v.x == id || v.y == id || v.z == id || v.w == id; }
+__device__ inline int bucket_free(uint4 v) {
+  return (int)(v.x == kEmpty) + (int)(v.y == kEmpty) + (int)(v.z == kEmpty) + (int)(v.w == kEmpty);
+}
+// 1 inserted (first visit), 0 present, 3 both buckets full (the id belongs
+// in the spill table). `bbits` = log2(buckets). Lanes insert distinct ids;
+// a lost atomicCAS means another lane filled one of this id's (at most 8)
+// slots, so nine rounds always reach a verdict.
+__device__ inline int shared_insert2(uint32_t* t, uint32_t bbits, uint32_t id) {
+  const uint32_t b1 = hash_slot(id, bbits), b2 = hash2_slot(id, bbits);
+  for (int it = 0; it < 9; ++it) {
+    const uint4 v1 = *(const uint4*)(t + 4 * b1);
+    const uint4 v2 = *(const uint4*)(t + 4 * b2);
+    if (bucket_has(v1, id) || bucket_has(v2, id)) return 0;
+    const int n1 = bucket_free(v1), n2 = bucket_free(v2);
+    if (n1 + n2 == 0) return 3;
+    const uint4 v = n1 >= n2 ? v1 : v2;
+    const uint32_t b = n1 >= n2 ? b1 : b2;
+    const int e = v.x == kEmpty ? 0 : v.y == kEmpty ? 1 : v.z == kEmpty ? 2 : 3;
+    if (atomicCAS(t + 4 * b + e, kEmpty, id) == kEmpty) return 1;
+  }
+  return 3;
+}
+__device__ inline bool shared_has2(const uint32_t* t, uint32_t bbits, uint32_t id) {
+  const uint4 v1 = *(const uint4*)(t + 4 * hash_slot(id, bbits));
+  const uint4 v2 = *(const uint4*)(t + 4 * hash2_slot(id, bbits));
+  return bucket_has(v1, id) || bucket_has(v2, id);
+}
+
 // Level B of the visited set (outlier queries only): look up level A, then
 // insert into B. Out of line to keep the common path compact.
 __device__ __noinline__ bool probe_level_b(uint32_t* spill_a, uint32_t* spill_b, uint32_t bits_a, uint32_t id) {
@@ -523,7 +568,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
   uint32_t* spill = a.spill ? a.spill + ((size_t)slot << a.spill_bits) : nullptr;
   uint32_t* spill_b = a.spill ? a.spill + (a.n_slots << a.spill_bits) + ((size_t)slot << (a.spill_bits + 3)) : nullptr;
   const uint32_t H = 1u << a.hash_bits;
-  const uint32_t h_limit = (H >> 2) * 3;
+  const uint32_t h_limit = H - (H >> 3);  // two-choice buckets stay short-probed to 7/8 load
   const uint32_t S = 1u << a.spill_bits;
   const uint32_t s_limit = (S >> 2) * 3;
   const uint32_t SB = S << 3;
@@ -636,7 +681,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       int level = 0;
       uint32_t tcount = 0, scount = 0;
       // 4. entry
-      if (lane == 0) probe_insert<true>(s.ht, a.hash_bits, entry, true);
+      if (lane == 0) shared_insert2(s.ht, a.hash_bits - 2, entry);
       tcount = 1;
       if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
       vcount = 1;
@@ -656,37 +701,40 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       sz = 1;
       __syncwarp();
       int cursor = 0;
-      uint32_t pref_node = kSent;
-      uint32_t pref_row[4];
+      uint32_t pref_node = kSent;  // node whose row was prefetched into rowbuf[pbuf]
+      int pbuf = 0;
       const uint32_t RL = a.r_pad >> 5;
 
       while (cursor < sz) {
         const uint32_t node = s.pool_id[cursor];
         __syncwarp();
         if (lane == 0) s.pool_id[cursor] = node | kChecked;
-        __syncwarp();
         ++expansions;
-        // neighbours (the row of the next pool entry is prefetched speculatively)
+        // neighbours: the row of the predicted expansion was prefetched into
+        // rowbuf (cp.async); every prefetch has landed after this wait
+        cp_async_wait_all();
+        __syncwarp();
         uint32_t row[4];
         if (node == pref_node) {
+          const uint32_t* rb = s.rowbuf + pbuf * a.r_pad + lane;
 #pragma unroll
-          for (int r = 0; r < 4; ++r) row[r] = pref_row[r];
+          for (int r = 0; r < 4; ++r) row[r] = (uint32_t)r < RL ? rb[32 * r] : kSent;
         } else {
           const uint32_t* rg = a.adj + (size_t)node * a.r_pad + lane;
 #pragma unroll
           for (int r = 0; r < 4; ++r) row[r] = (uint32_t)r < RL ? __ldg(rg + 32 * r) : kSent;
         }
+        __syncwarp();  // both buffers read before new copies are issued
         const int nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
-        {
-          if (nxt < sz) {
-            pref_node = s.pool_id[nxt] & ~kChecked;
-            const uint32_t* pg = a.adj + (size_t)pref_node * a.r_pad + lane;
-#pragma unroll
-            for (int r = 0; r < 4; ++r) pref_row[r] = (uint32_t)r < RL ? __ldg(pg + 32 * r) : kSent;
-          } else {
-            pref_node = kSent;
-          }
+        // next expansion if nothing lands before it: prefetch into buffer 0
+        if (nxt < sz) {
+          pref_node = s.pool_id[nxt] & ~kChecked;
+          prefetch_row(a.adj, a.r_pad, s.rowbuf, pref_node, lane);
+          pbuf = 0;
+        } else {
+          pref_node = kSent;
         }
+        bool early = false;  // buffer 1 holds (or is receiving) a prediction of this expansion
         bool ended = false;  // first SENTINEL seen: degree reached
         bool overflow = false;
         int first_insert = 0x7fffffff;
@@ -734,15 +782,30 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
           bool is_new = false;
           // every id lives in exactly one level; insert into the current one
           if (level == 0) {
-            if (valid) is_new = probe_insert<true>(s.ht, a.hash_bits, id, true) == 1;
+            const int r = valid ? shared_insert2(s.ht, a.hash_bits - 2, id) : 0;
+            is_new = r == 1;
+            const bool to_spill = r == 3;  // both buckets full: this id starts level A
+            if (__any_sync(kFull, to_spill)) {
+              if (spill == nullptr) {
+                overflow = true;
+                break;
+              }
+              for (uint32_t i = lane * 4; i < S; i += 128)
+                *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+              __syncwarp();
+              level = 1;
+              const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
+              const uint4 sv = to_spill ? __ldcv((const uint4*)(spill + 4 * sbk)) : make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+              is_new |= spill_insert_warp(spill, a.spill_bits, id, to_spill, sbk, sv, lane);
+            }
           } else if (level == 1) {
             // home bucket of level A read before the shared lookup: the two overlap
             const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
             uint4 sv = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
             if (valid) sv = __ldcv((const uint4*)(spill + 4 * sbk));
-            const bool need = valid && probe_insert<true>(s.ht, a.hash_bits, id, false) == 2;
+            const bool need = valid && !shared_has2(s.ht, a.hash_bits - 2, id);
             is_new = spill_insert_warp(spill, a.spill_bits, id, need, sbk, sv, lane);
-          } else if (valid && probe_insert<true>(s.ht, a.hash_bits, id, false) == 2) {
+          } else if (valid && !shared_has2(s.ht, a.hash_bits - 2, id)) {
             is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
           }
           const uint32_t newm = __ballot_sync(kFull, is_new);
@@ -789,37 +852,55 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
               cpos = lo;
             }
             const int start = (int)__reduce_min_sync(kFull, (unsigned)cpos);
-            uint32_t pd[PT], pi[PT];
-            int np[PT];
-            bool pv[PT];  // this lane's pool slot t holds an entry that may move
-#pragma unroll
-            for (int t = 0; t < PT; ++t) {
-              const int p = lane + 32 * t;
-              pv[t] = p >= start && p < sz;
-              pd[t] = pv[t] ? s.pool_d[p] : 0u;
-              pi[t] = pv[t] ? s.pool_id[p] : 0u;
-              np[t] = p;  // + (# accepted candidates closer), at most p + 32
+            if (start <= min(nxt, first_insert)) {
+              // the closest accepted candidate lands before every unexpanded
+              // entry, so it is the next expansion: fetch its row now, while
+              // the merge runs
+              const uint32_t dmin = __reduce_min_sync(kFull, acc ? my_d : 0xffffffffu);
+              pref_node = __shfl_sync(kFull, id, __ffs(__ballot_sync(kFull, acc && my_d == dmin)) - 1);
+              if (early) {  // rows longer than 32: a later segment overrides; let the earlier copy land
+                cp_async_wait_all();
+                __syncwarp();
+              }
+              prefetch_row(a.adj, a.r_pad, s.rowbuf + a.r_pad, pref_node, lane);
+              pbuf = 1;
+              early = true;
             }
-            // one pass over the accepted candidates (adjacency order): rank
-            // among them by (distance, lane) and the shift of each pool entry
+            // rank among the accepted candidates by (distance, lane): the
+            // reference inserts them one by one in adjacency order and an
+            // equal distance goes after, so equal candidates keep lane order
             int crank = 0;
-            uint32_t m = am;
-            while (m) {
+            for (uint32_t m = am; m; m &= m - 1) {
               const int jl = __ffs(m) - 1;
-              m &= m - 1;
               const uint32_t dj = __shfl_sync(kFull, my_d, jl);
               crank += (dj < my_d) | ((dj == my_d) & (jl < lane));
-#pragma unroll
-              for (int t = 0; t < PT; ++t) np[t] += (int)(pv[t] && dj < pd[t]);
             }
-            if (acc) cpos += crank;
-            __syncwarp();
-#pragma unroll
-            for (int t = 0; t < PT; ++t) {
-              if (pv[t] && np[t] < (int)ef) {
-                s.pool_d[np[t]] = pd[t];
-                s.pool_id[np[t]] = pi[t];
+            if (acc) cpos += crank;  // final slot; >= ef: falls off the end
+            const int nsz = min(sz + na, (int)ef);
+            // Pool entries move right past the candidate slots. Output slot j
+            // (not a candidate slot) takes old entry j - #(candidate slots < j);
+            // chunks of 32 slots from the top down, so a chunk's sources (all
+            // <= its slots) are read before a lower chunk is written.
+            for (int t = PT - 1; t >= 0; --t) {
+              const int base = 32 * t;
+              if (base >= nsz || base + 32 <= start) continue;
+              const uint32_t cw =
+                  __reduce_or_sync(kFull, (acc && cpos >= base && cpos < base + 32) ? 1u << (cpos - base) : 0u);
+              const int below = __popc(__ballot_sync(kFull, acc && cpos < base));
+              const int j = base + lane;
+              const bool mv = j >= start && j < nsz && !((cw >> lane) & 1u);
+              uint32_t vd = 0, vi = 0;
+              if (mv) {
+                const int src = j - below - __popc(cw & lanemask_lt(lane));
+                vd = s.pool_d[src];
+                vi = s.pool_id[src];
               }
+              __syncwarp();
+              if (mv) {
+                s.pool_d[j] = vd;
+                s.pool_id[j] = vi;
+              }
+              __syncwarp();
             }
             if (acc && cpos < (int)ef) {
               s.pool_d[cpos] = my_d;
