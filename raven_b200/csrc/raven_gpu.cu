@@ -315,46 +315,37 @@ __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float
 // ---------------------------------------------------------------------------
 // Search launch.
 // ---------------------------------------------------------------------------
-template <int QUANT, int CPL, int PT>
+template <int QUANT, int CPL>
 cudaError_t launch_t(const SearchArgs& a, uint32_t smem_per_block, int grid, cudaStream_t st) {
-  auto k = search_kernel<QUANT, CPL, PT>;
+  auto k = a.pool_cap <= 64 ? search_kernel<QUANT, CPL, 64> : search_kernel<QUANT, CPL, 0>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
   if (e != cudaSuccess) return e;
   k<<<grid, kWarpsPerBlock * 32, smem_per_block, st>>>(a);
   return cudaGetLastError();
 }
-template <int QUANT, int CPL, int PT>
-cudaError_t occupancy_t(uint32_t smem_per_block, int* blocks) {
-  auto k = search_kernel<QUANT, CPL, PT>;
+template <int QUANT, int CPL>
+cudaError_t occupancy_t(uint32_t pool_cap, uint32_t smem_per_block, int* blocks) {
+  auto k = pool_cap <= 64 ? search_kernel<QUANT, CPL, 64> : search_kernel<QUANT, CPL, 0>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, kWarpsPerBlock * 32, smem_per_block);
 }
 
-template <int QUANT, int CPL>
-cudaError_t dispatch_pt(int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st, int* blocks) {
-  switch (pt) {
-    case 2: return occ ? occupancy_t<QUANT, CPL, 2>(smem, blocks) : launch_t<QUANT, CPL, 2>(a, smem, grid, st);
-    case 4: return occ ? occupancy_t<QUANT, CPL, 4>(smem, blocks) : launch_t<QUANT, CPL, 4>(a, smem, grid, st);
-    case 8: return occ ? occupancy_t<QUANT, CPL, 8>(smem, blocks) : launch_t<QUANT, CPL, 8>(a, smem, grid, st);
-  }
-  return cudaErrorInvalidValue;
-}
 template <int QUANT>
-cudaError_t dispatch_cpl(int cpl, int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
+cudaError_t dispatch_cpl(int cpl, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
                          int* blocks) {
   switch (cpl) {
-    case 1: return dispatch_pt<QUANT, 1>(pt, occ, a, smem, grid, st, blocks);
-    case 2: return dispatch_pt<QUANT, 2>(pt, occ, a, smem, grid, st, blocks);
-    case 4: return dispatch_pt<QUANT, 4>(pt, occ, a, smem, grid, st, blocks);
-    case 8: return dispatch_pt<QUANT, 8>(pt, occ, a, smem, grid, st, blocks);
+    case 1: return occ ? occupancy_t<QUANT, 1>(a.pool_cap, smem, blocks) : launch_t<QUANT, 1>(a, smem, grid, st);
+    case 2: return occ ? occupancy_t<QUANT, 2>(a.pool_cap, smem, blocks) : launch_t<QUANT, 2>(a, smem, grid, st);
+    case 4: return occ ? occupancy_t<QUANT, 4>(a.pool_cap, smem, blocks) : launch_t<QUANT, 4>(a, smem, grid, st);
+    case 8: return occ ? occupancy_t<QUANT, 8>(a.pool_cap, smem, blocks) : launch_t<QUANT, 8>(a, smem, grid, st);
   }
   return cudaErrorInvalidValue;
 }
-cudaError_t dispatch(int quant, int cpl, int pt, bool occ, const SearchArgs& a, uint32_t smem, int grid,
-                     cudaStream_t st, int* blocks) {
-  return quant == 0 ? dispatch_cpl<0>(cpl, pt, occ, a, smem, grid, st, blocks)
-                    : dispatch_cpl<1>(cpl, pt, occ, a, smem, grid, st, blocks);
+cudaError_t dispatch(int quant, int cpl, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
+                     int* blocks) {
+  return quant == 0 ? dispatch_cpl<0>(cpl, occ, a, smem, grid, st, blocks)
+                    : dispatch_cpl<1>(cpl, occ, a, smem, grid, st, blocks);
 }
 
 constexpr uint32_t kMaxEf = 256;
@@ -380,7 +371,8 @@ std::vector<uint32_t> ef_table(uint32_t S, uint32_t min_ef, uint32_t max_ef, flo
 }
 
 struct Plan {
-  int quant, cpl, pt, hash_bits, spill_bits;
+  int quant, cpl, hash_bits, spill_bits;
+  uint32_t pool_cap;  // beam pool entries per warp: ef_cap rounded up to 32
   uint32_t ef_cap;
   uint32_t smem_warp, smem_block;
   std::vector<uint32_t> table;
@@ -414,7 +406,7 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   }
   if (ef_cap > kMaxEf) return fail(RAVEN_ELIMIT, "ef above the engine limit of 256");
   pl->ef_cap = ef_cap;
-  pl->pt = ef_cap <= 64 ? 2 : ef_cap <= 128 ? 4 : 8;
+  pl->pool_cap = ef_cap <= 64 ? 64u : (ef_cap + 31) & ~31u;  // <= 64: the fixed-layout kernel
   uint32_t hb = ix->hash_bits_override;
   if (hb == 0) {
     // Shared-memory visited slots per warp. Past 3/4 load a query continues
@@ -430,7 +422,7 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   // the visited table doubles as the row staging area: it must hold a row
   while ((1u << hb) < ix->dim_pad) ++hb;
   pl->hash_bits = (int)hb;
-  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pt, hb, ix->r_pad);
+  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pool_cap, hb, ix->r_pad);
   pl->smem_block = pl->smem_warp * kWarpsPerBlock;
   return RAVEN_OK;
 }
@@ -452,7 +444,9 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   if (!o || !o->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
   CU(cudaSetDevice(ix->device));
   int blocks_per_sm = 0;
-  CU(dispatch(pl.quant, pl.cpl, pl.pt, true, SearchArgs{}, pl.smem_block, 0, st, &blocks_per_sm));
+  SearchArgs occ_args{};
+  occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
+  CU(dispatch(pl.quant, pl.cpl, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
   if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
   uint64_t grid64 = (uint64_t)blocks_per_sm * ix->num_sms;
   uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
@@ -482,6 +476,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.vec_rem = ix->dim % 16;
   a.adj = ix->d_adj;
   a.r_pad = ix->r_pad;
+  a.pool_cap = pl.pool_cap;
   a.codes = ix->d_codes[pl.quant];
   a.code_stride = ix->q_stride[pl.quant];
   a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
@@ -533,7 +528,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.hist_len = o->history_len;
   a.counter = counter;
   a.nav_only = nav_only;
-  e = dispatch(pl.quant, pl.cpl, pl.pt, false, a, pl.smem_block, grid, st, nullptr);
+  e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
   cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
   return RAVEN_OK;
@@ -1067,7 +1062,9 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   const size_t per_slot = (9ull << sb) * 4;
   const uint64_t max_slots = (kNoAllocScratchBytes - kNoAllocHeader) / per_slot;
   int blocks_per_sm = 0;
-  CU(dispatch(pl.quant, pl.cpl, pl.pt, true, SearchArgs{}, pl.smem_block, 0, st, &blocks_per_sm));
+  SearchArgs occ_args{};
+  occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
+  CU(dispatch(pl.quant, pl.cpl, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
   if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
   const uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
   const uint64_t grid64 = std::min<uint64_t>({(uint64_t)blocks_per_sm * ix->num_sms, need, max_slots / kWarpsPerBlock});
@@ -1090,6 +1087,7 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   a.vec_rem = ix->dim % 16;
   a.adj = ix->d_adj;
   a.r_pad = ix->r_pad;
+  a.pool_cap = pl.pool_cap;
   a.codes = ix->d_codes[pl.quant];
   a.code_stride = ix->q_stride[pl.quant];
   a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
@@ -1140,7 +1138,7 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   a.hist_len = o->history_len;
   a.counter = counter;
   a.nav_only = 0;
-  const cudaError_t e = dispatch(pl.quant, pl.cpl, pl.pt, false, a, pl.smem_block, grid, st, nullptr);
+  const cudaError_t e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
   return RAVEN_OK;
 }

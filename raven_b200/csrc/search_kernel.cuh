@@ -46,6 +46,7 @@ struct SearchArgs {
   uint32_t vec_rem;  // dim % 16
   const uint32_t* __restrict__ adj;
   uint32_t r_pad;  // row stride in ids (multiple of 32)
+  uint32_t pool_cap;  // beam pool capacity per warp (multiple of 32, >= every query's ef)
   const uint8_t* __restrict__ codes;
   uint32_t code_stride;  // bytes per code row (power of two, >= 16)
   const float* __restrict__ q_inv;
@@ -95,8 +96,8 @@ struct SearchArgs {
 struct WarpSmem {
   float* qf;          // dim_pad floats, lane-major
   uint8_t* qcode;     // code_stride bytes
-  uint32_t* pool_d;   // 32*PT
-  uint32_t* pool_id;  // 32*PT
+  uint32_t* pool_d;   // pool_cap
+  uint32_t* pool_id;  // pool_cap
   uint32_t* cand_id;  // 32
   uint32_t* cand_d;   // 32
   float* nd;          // 32
@@ -106,13 +107,13 @@ struct WarpSmem {
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
-__host__ __device__ inline uint32_t warp_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pt,
+__host__ __device__ inline uint32_t warp_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pool_cap,
                                                     uint32_t hash_bits, uint32_t r_pad) {
-  return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(32 * pt * 4) + 3 * 128 + 2 * r_pad * 4 +
+  return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(pool_cap * 4) + 3 * 128 + 2 * r_pad * 4 +
          align16((1u << hash_bits) * 4);
 }
 
-__device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, int pt) {
+__device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, uint32_t pool_cap) {
   WarpSmem s;
   uint32_t o = 0;
   s.qf = (float*)(base + o);
@@ -120,9 +121,9 @@ __device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, int pt) {
   s.qcode = base + o;
   o += align16(a.code_stride);
   s.pool_d = (uint32_t*)(base + o);
-  o += align16(32 * pt * 4);
+  o += align16(pool_cap * 4);
   s.pool_id = (uint32_t*)(base + o);
-  o += align16(32 * pt * 4);
+  o += align16(pool_cap * 4);
   s.cand_id = (uint32_t*)(base + o);
   o += 128;
   s.cand_d = (uint32_t*)(base + o);
@@ -557,12 +558,15 @@ struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
 // ---------------------------------------------------------------------------
 // The search kernel.
 // ---------------------------------------------------------------------------
-template <int QUANT, int CPL, int PT>
+// POOLMAX: 64 for pools of at most 64 entries (layout and merge bounds fixed
+// at compile time), 0 for a run-time capacity (a.pool_cap).
+template <int QUANT, int CPL, int POOLMAX>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
-  const WarpSmem s = carve(smem_raw + (size_t)wib * a.smem_per_warp, a, PT);
+  const uint32_t pool_cap = POOLMAX ? (uint32_t)POOLMAX : a.pool_cap;
+  const WarpSmem s = carve(smem_raw + (size_t)wib * a.smem_per_warp, a, pool_cap);
   const uint32_t slot = blockIdx.x * kWarpsPerBlock + wib;
   // level A tables are contiguous (hot, L2/TLB friendly); level B only for outliers
   uint32_t* spill = a.spill ? a.spill + ((size_t)slot << a.spill_bits) : nullptr;
@@ -651,7 +655,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       }
       ef = max(e, a.k);
     }
-    if (ef == 0 || ef > 32u * PT) status = 3;  // RAVEN_Q_BAD_EF (host validation makes this unreachable)
+    if (ef == 0 || ef > pool_cap) status = 3;  // RAVEN_Q_BAD_EF (host validation makes this unreachable)
 
     uint32_t vcount = 0, expansions = 0;
     int sz = 0;
@@ -881,9 +885,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
             // (not a candidate slot) takes old entry j - #(candidate slots < j);
             // chunks of 32 slots from the top down, so a chunk's sources (all
             // <= its slots) are read before a lower chunk is written.
-            for (int t = PT - 1; t >= 0; --t) {
+            // the chunks holding [start, nsz), top down (fixed bounds for small pools)
+            const int t_lo = POOLMAX ? 0 : start >> 5;
+            const int t_hi = POOLMAX ? POOLMAX / 32 - 1 : (nsz - 1) >> 5;
+#pragma unroll
+            for (int t = t_hi; t >= t_lo; --t) {
               const int base = 32 * t;
-              if (base >= nsz || base + 32 <= start) continue;
+              if (POOLMAX && (base >= nsz || base + 32 <= start)) continue;
               const uint32_t cw =
                   __reduce_or_sync(kFull, (acc && cpos >= base && cpos < base + 32) ? 1u << (cpos - base) : 0u);
               const int below = __popc(__ballot_sync(kFull, acc && cpos < base));
