@@ -8,7 +8,9 @@
 //             SQ4, 128 B for dim 128 SQ8), zero padded past the real code
 //   nav       slot[n] -> nav_off[slot..slot+1] into nav_edges (global ids)
 //   adaptive  sorted sample distances (<= 2000) + per-call rank->ef table
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <cmath>
@@ -21,6 +23,7 @@
 
 #include "../../include/raven_gpu.h"
 #include "host_index.h"
+#include "knn_tc.cuh"
 #include "search_kernel.cuh"
 
 using namespace raven_dev;
@@ -271,6 +274,91 @@ __global__ void knn_merge_kernel(const uint32_t* __restrict__ in_i, const float*
       out_i[qi * k + rank] = id;
       out_d[qi * k + rank] = d;
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core exact kNN: operand preparation (knn_tc.cuh holds the kernel).
+// ---------------------------------------------------------------------------
+// TF32 value of x, rounded to nearest (ties away), low 13 bits zero.
+__device__ inline float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// flags[0] bit 0: a value not exact in TF32 (non-integer or |v| > 2048);
+// flags[1], flags[2]: largest base / query squared norm (f32 bits).
+__device__ inline bool tf32_exact_int(float v) { return v == rintf(v) && fabsf(v) <= 2048.0f; }
+
+// One warp per base row: squared norm and exactness flags; rows n..n_pad-1
+// get +inf (rows past the base never qualify as neighbours).
+__global__ void tc_base_norms_kernel(const float* __restrict__ vec, uint64_t n, uint64_t n_pad, uint32_t dim,
+                                     float* __restrict__ xn, unsigned* __restrict__ flags) {
+  const uint64_t row = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n_pad) return;
+  if (row >= n) {
+    if (lane == 0) xn[row] = __int_as_float(0x7f800000);
+    return;
+  }
+  const float* v = vec + row * dim;
+  float acc = 0.0f;
+  bool inexact = false;
+  for (uint32_t j = lane; j < dim; j += 32) {
+    const float x = v[j];
+    acc = fmaf(x, x, acc);
+    inexact |= !tf32_exact_int(x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (__any_sync(0xffffffffu, inexact) && lane == 0) atomicOr(&flags[0], 1u);
+  if (lane == 0) {
+    xn[row] = acc;
+    atomicMax(&flags[1], __float_as_uint(acc));
+  }
+}
+
+// One warp per query: the row in the base rows' lane-major order (position
+// p < 16C holds element 16*(p%C) + p/C), zero-padded to kpad, split into
+// TF32 hi and lo parts, its squared norm and the exactness flags. Rows
+// nq..nq_pad-1 are zero.
+__global__ void tc_query_prep_kernel(const float* __restrict__ q, uint64_t nq, uint64_t nq_pad, uint32_t dim,
+                                     uint32_t C, uint32_t kpad, float* __restrict__ qh, float* __restrict__ ql,
+                                     float* __restrict__ qn, unsigned* __restrict__ flags) {
+  const uint64_t row = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= nq_pad) return;
+  float acc = 0.0f;
+  bool inexact = false;
+  for (uint32_t p = lane; p < kpad; p += 32) {
+    float x = 0.0f;
+    if (row < nq && p < dim) {
+      const uint32_t e = p < 16 * C ? 16 * (p % C) + p / C : p;
+      x = q[row * dim + e];
+    }
+    acc = fmaf(x, x, acc);
+    inexact |= !tf32_exact_int(x);
+    const float h = tf32_round(x);
+    qh[row * kpad + p] = h;
+    ql[row * kpad + p] = x - h;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (__any_sync(0xffffffffu, inexact) && lane == 0) atomicOr(&flags[0], 1u);
+  if (lane == 0 && row < nq) {
+    qn[row] = acc;
+    atomicMax(&flags[2], __float_as_uint(acc));
+  }
+}
+
+// Base hi/lo split for the three-pass form.
+__global__ void tc_base_split_kernel(const float* __restrict__ vec, uint64_t total, float* __restrict__ xh,
+                                     float* __restrict__ xl) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += (uint64_t)gridDim.x * blockDim.x) {
+    const float x = vec[i];
+    const float h = tf32_round(x);
+    xh[i] = h;
+    xl[i] = x - h;
   }
 }
 
@@ -939,6 +1027,75 @@ int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven
   return RAVEN_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// cuTensorMapEncodeTiled, looked up once through the runtime (no link-time
+// dependency on the driver library).
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    else
+      (void)cudaGetLastError();
+  });
+  return fn;
+}
+
+// f32 matrix of `rows` rows, `cols` used columns, row stride `ld` floats
+// (ld * 4 a multiple of 16 bytes); box 32 columns x 128 rows, 128-byte
+// swizzle (the K-major SW128 operand layout), out-of-range elements read 0.
+bool make_tile_map(CUtensorMap* m, const float* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+  PFN_cuTensorMapEncodeTiled_v12000 f = encode_tiled();
+  if (!f) return false;
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)raven_tc::kBK, (cuuint32_t)raven_tc::kBM};
+  cuuint32_t estr[2] = {1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int PASSES, int KT>
+cudaError_t launch_knn_tc(const CUtensorMap& qh, const CUtensorMap& ql, const CUtensorMap& xh, const CUtensorMap& xl,
+                          const raven_tc::Params& p, unsigned grid, cudaStream_t st) {
+  auto kern = raven_tc::knn_tc_kernel<PASSES, KT>;
+  const int smem = (int)raven_tc::Layout<PASSES>::kBytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, raven_tc::kThreads, smem, st>>>(qh, ql, xh, xl, p);
+  return cudaGetLastError();
+}
+
+// Splits of the base range: as many CTAs as keep the last wave full, at
+// least 8 base tiles per CTA.
+uint64_t tc_splits(uint64_t n, uint64_t qtiles, int sms) {
+  const uint64_t tiles = (n + raven_tc::kBN - 1) / raven_tc::kBN;
+  uint64_t best = 1;
+  double best_eff = -1.0;
+  for (uint64_t s = 1; s <= 64 && s * 8 <= std::max<uint64_t>(tiles, 8); ++s) {
+    const uint64_t items = qtiles * s;
+    const uint64_t waves = (items + sms - 1) / sms;
+    const double eff = (double)items / (double)(waves * sms) - 0.002 * (double)s;  // prefer fewer merges
+    if (eff > best_eff) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+extern "C" {
+
 int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint32_t k, uint32_t* d_ids,
                            float* d_dists, void* stream) {
   if (!ix || (!d_q && nq) || !d_ids || !d_dists) return fail(RAVEN_EINVAL, "null argument");
@@ -946,6 +1103,101 @@ int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint3
   if (nq == 0) return RAVEN_OK;
   CU(cudaSetDevice(ix->device));
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
+  const uint32_t dim = ix->dim;
+  const bool tc = dim % 4 == 0 && dim <= (uint32_t)(raven_tc::kBK * raven_tc::kMaxKB) && encode_tiled() != nullptr;
+  if (tc) {
+    // tensor-core path (knn_tc.cuh): prepare operands, pick one or three passes
+    const uint32_t kb = (dim + raven_tc::kBK - 1) / raven_tc::kBK, kpad = kb * raven_tc::kBK;
+    const uint64_t qtiles = (nq + raven_tc::kBM - 1) / raven_tc::kBM, nq_pad = qtiles * raven_tc::kBM;
+    const uint64_t splits = tc_splits(ix->n, qtiles, ix->num_sms);
+    uint64_t split_rows = (ix->n + splits - 1) / splits;
+    split_rows = (split_rows + raven_tc::kBN - 1) / raven_tc::kBN * raven_tc::kBN;
+    const uint64_t nsplit = (ix->n + split_rows - 1) / split_rows;
+    const size_t qbytes = nq_pad * kpad * 4, per = nsplit * nq * k;
+    const uint64_t n_pad = (ix->n + raven_tc::kBN - 1) / raven_tc::kBN * raven_tc::kBN;
+    const size_t bytes = 2 * qbytes + nq_pad * 4 + n_pad * 4 + 16 + per * 8;
+    uint8_t* tmp = nullptr;
+    CU(cudaMallocAsync((void**)&tmp, bytes, st));
+    float* qh = (float*)tmp;
+    float* ql = (float*)(tmp + qbytes);
+    float* qn = (float*)(tmp + 2 * qbytes);
+    float* xn = qn + nq_pad;
+    unsigned* flags = (unsigned*)(xn + n_pad);
+    uint32_t* ti = (uint32_t*)(flags + 4);
+    float* td = (float*)(ti + per);
+    float* xsplit = nullptr;
+    int* d_err = (int*)(flags + 3);
+    unsigned h_flags[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemsetAsync(flags, 0, 16, st);
+    if (e == cudaSuccess) {
+      tc_base_norms_kernel<<<(unsigned)((n_pad * 32 + 255) / 256), 256, 0, st>>>(ix->d_vec, ix->n, n_pad, dim, xn,
+                                                                                 flags);
+      tc_query_prep_kernel<<<(unsigned)((nq_pad * 32 + 255) / 256), 256, 0, st>>>(d_q, nq, nq_pad, dim, dim / 16, kpad,
+                                                                                    qh, ql, qn, flags);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(h_flags, flags, 16, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    int passes = 3;
+    if (e == cudaSuccess) {
+      float mx, mq;
+      std::memcpy(&mx, &h_flags[1], 4);
+      std::memcpy(&mq, &h_flags[2], 4);
+      // exact in one pass: TF32-exact integers, norms and their sum below 2^24
+      if (!(h_flags[0] & 1u) && (double)mx + (double)mq < 16777216.0) passes = 1;
+    }
+    if (e == cudaSuccess && passes == 3) {
+      e = cudaMallocAsync((void**)&xsplit, ix->n * dim * 8, st);
+      if (e == cudaSuccess) {
+        tc_base_split_kernel<<<(unsigned)std::min<uint64_t>((ix->n * dim + 255) / 256, 65535u * 4), 256, 0, st>>>(
+            ix->d_vec, ix->n * dim, xsplit, xsplit + ix->n * dim);
+        e = cudaGetLastError();
+      }
+    }
+    if (e == cudaSuccess) {
+      CUtensorMap m_qh, m_ql, m_xh, m_xl;
+      const float* xh = passes == 1 ? ix->d_vec : xsplit;
+      const float* xl = passes == 1 ? ix->d_vec : xsplit + ix->n * dim;
+      bool ok = make_tile_map(&m_qh, qh, kpad, nq_pad, kpad) && make_tile_map(&m_ql, ql, kpad, nq_pad, kpad) &&
+                make_tile_map(&m_xh, xh, dim, ix->n, dim) && make_tile_map(&m_xl, xl, dim, ix->n, dim);
+      if (!ok) {
+        e = cudaErrorInvalidValue;
+      } else {
+        raven_tc::Params prm{};
+        prm.n = ix->n;
+        prm.nq = nq;
+        prm.kb = kb;
+        prm.k = k;
+        prm.split_rows = split_rows;
+        prm.qtiles = (uint32_t)qtiles;
+        prm.xn = xn;
+        prm.qn = qn;
+        prm.out_i = ti;
+        prm.out_d = td;
+        prm.err = d_err;
+        const unsigned grid = (unsigned)(qtiles * nsplit);
+        if (passes == 1)
+          e = k <= 16 ? launch_knn_tc<1, 16>(m_qh, m_ql, m_xh, m_xl, prm, grid, st)
+                      : launch_knn_tc<1, 32>(m_qh, m_ql, m_xh, m_xl, prm, grid, st);
+        else
+          e = k <= 16 ? launch_knn_tc<3, 16>(m_qh, m_ql, m_xh, m_xl, prm, grid, st)
+                      : launch_knn_tc<3, 32>(m_qh, m_ql, m_xh, m_xl, prm, grid, st);
+      }
+    }
+    if (e == cudaSuccess) {
+      knn_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(ti, td, (uint32_t)nsplit, nq, k, d_ids, d_dists);
+      e = cudaGetLastError();
+    }
+    int h_err = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, d_err, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (xsplit) cudaFreeAsync(xsplit, st);
+    cudaFreeAsync(tmp, st);
+    if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("knn (tensor cores): ") + cudaGetErrorString(e));
+    if (h_err) return fail(RAVEN_ECUDA, "knn (tensor cores): a pipeline wait ran out");
+    return RAVEN_OK;
+  }
+  // CUDA-core path (dims the tensor-core path does not take)
   const uint64_t qblocks = (nq + KQ - 1) / KQ;
   uint64_t splits = std::max<uint64_t>(1, (uint64_t)ix->num_sms * 4 / std::max<uint64_t>(qblocks, 1));
   splits = std::min<uint64_t>(splits, (ix->n + KB - 1) / KB);
