@@ -34,7 +34,8 @@ constexpr int kBM = 128;      // queries per tile = tensor-memory lanes
 constexpr int kBN = 128;      // base rows per tile = accumulator columns
 constexpr int kBK = 32;       // floats per K block: one 128-byte swizzled row
 constexpr int kMaxKB = 4;     // K blocks: dim <= 128
-constexpr int kThreads = 256;
+constexpr int kEpiWarps = 8;  // two per lane quadrant: columns 0-63 and 64-127 of a tile
+constexpr int kThreads = 32 * (4 + kEpiWarps);
 constexpr uint32_t kBlockBytes = kBN * kBK * 4;  // one operand block: 16 KB
 constexpr uint32_t kTmemCols = 2 * kBN;
 constexpr long long kWaitCycles = 1ll << 32;     // ~2 s: a longer wait is a fault
@@ -61,7 +62,7 @@ struct Params {
   uint32_t qtiles;      // query tiles
   const float* xn;      // base squared norms, +inf from row n up to a multiple of kBN
   const float* qn;      // query squared norms
-  uint32_t* out_i;      // [split][nq][k]
+  uint32_t* out_i;      // [split][column half][nq][k]
   float* out_d;
   int* err;             // set to 1 when a wait ran out
 };
@@ -134,6 +135,55 @@ __device__ inline void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// 32 dot products of one query against base rows id0..id0+31: distances
+// |q|^2 + |x|^2 - 2 q.x, and any that beat the current k-th distance go into
+// the sorted list. The common case (nothing qualifies) costs an FMA and a
+// min per element; insertions use one compact site, the candidate's value
+// picked by a select chain (no dynamic register indexing). Ids rise along the
+// scan, so an equal distance never displaces an entry already held and the
+// strict test keeps ties ordered by id.
+template <int KT>
+__device__ inline void scan_chunk(const uint32_t (&v)[32], const float* xn, float qnorm, uint32_t id0, uint32_t k,
+                                  float (&kd)[KT], uint32_t (&ki)[KT], float& thr) {
+  const float4* xp = (const float4*)xn;
+  float dv[32];
+  float dmin = __int_as_float(0x7f800000);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 f = __ldg(xp + j);
+    dv[4 * j] = fmaf(-2.0f, __uint_as_float(v[4 * j]), qnorm + f.x);
+    dv[4 * j + 1] = fmaf(-2.0f, __uint_as_float(v[4 * j + 1]), qnorm + f.y);
+    dv[4 * j + 2] = fmaf(-2.0f, __uint_as_float(v[4 * j + 2]), qnorm + f.z);
+    dv[4 * j + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j + 3]), qnorm + f.w);
+    dmin = fminf(dmin, fminf(fminf(dv[4 * j], dv[4 * j + 1]), fminf(dv[4 * j + 2], dv[4 * j + 3])));
+  }
+  if (!(dmin < thr)) return;
+  uint32_t cand = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) cand |= (uint32_t)(dv[j] < thr) << j;
+  while (cand) {
+    const int j = __ffs(cand) - 1;
+    cand &= cand - 1;
+    float cd = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 32; ++m) cd = m == j ? dv[m] : cd;
+    if (!(cd < thr)) continue;  // an earlier insertion of this chunk raised the bar
+    uint32_t ci = id0 + (uint32_t)j;
+#pragma unroll
+    for (int m = 0; m < KT; ++m) {
+      const bool sw = cd < kd[m] || (cd == kd[m] && ci < ki[m]);
+      const float td = kd[m];
+      const uint32_t ti = ki[m];
+      kd[m] = sw ? cd : td;
+      ki[m] = sw ? ci : ti;
+      cd = sw ? td : cd;
+      ci = sw ? ti : ci;
+    }
+#pragma unroll
+    for (int m = 0; m < KT; ++m) thr = (uint32_t)m == k - 1 ? kd[m] : thr;
+  }
+}
+
 template <int PASSES, int KT>
 __global__ void __launch_bounds__(kThreads, 1)
     knn_tc_kernel(const __grid_constant__ CUtensorMap tm_qh, const __grid_constant__ CUtensorMap tm_ql,
@@ -170,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), 4);  // one arrive per epilogue warp
+      mbar_init(acc_empty(b), kEpiWarps);  // one arrive per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -252,8 +302,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) mma_commit(acc_full(b));
       }
     }
-  } else if (warp >= 4) {  // epilogue: thread r <-> query r of the tile <-> tensor-memory lane r
-    const int r = (warp - 4) * 32 + lane;
+  } else if (warp >= 4) {
+    // epilogue: warp w reads tensor-memory lanes 32*(w%4).. (query rows) and
+    // one half of each tile's columns; thread <-> (query r, column half)
+    const int quad = warp & 3, half = (warp - 4) >> 2;
+    const int r = quad * 32 + lane;
     const uint64_t qi = q0 + (uint64_t)r;
     const float qnorm = qi < p.nq ? p.qn[qi] : 0.0f;
     float kd[KT];
@@ -264,7 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ki[j] = 0xffffffffu;
     }
     float thr = __int_as_float(0x7f800000);  // distance of the k-th entry held
-    const uint32_t lane_base = (uint32_t)((warp - 4) * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    constexpr int kHalf = kBN / 2;
     for (uint32_t t = 0; t < ntiles; ++t) {
       const int b = (int)(t & 1u);
       const bool got = mbar_wait(acc_full(b), (t >> 1) & 1u);
@@ -274,60 +328,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint64_t row0 = r_begin + (uint64_t)t * kBN;
-      for (int c0 = 0; c0 < kBN; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)(b * kBN + c0), v);
-        // norms of these 32 base rows (+inf past row n: zero-filled rows never qualify)
-        const float4* xp = (const float4*)(p.xn + row0 + c0);
-        float xv[32];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 f = __ldg(xp + j);
-          xv[4 * j] = f.x;
-          xv[4 * j + 1] = f.y;
-          xv[4 * j + 2] = f.z;
-          xv[4 * j + 3] = f.w;
-        }
-        float dv[32];
-        uint32_t cand = 0;  // bit j: row c0+j beats the current k-th distance
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          dv[j] = fmaf(-2.0f, __uint_as_float(v[j]), qnorm + xv[j]);
-          cand |= (uint32_t)(dv[j] < thr) << j;
-        }
-        // Insertions are rare once the list is full: one compact insertion
-        // site, the candidate's value picked by a select chain (no dynamic
-        // register indexing). Ids rise along the scan, so an equal distance
-        // never displaces an entry already held and the strict test above
-        // keeps ties ordered by id.
-        while (cand) {
-          const int j = __ffs(cand) - 1;
-          cand &= cand - 1;
-          float cd = 0.0f;
-#pragma unroll
-          for (int m = 0; m < 32; ++m) cd = m == j ? dv[m] : cd;
-          if (!(cd < thr)) continue;  // an earlier insertion of this chunk raised the bar
-          uint32_t ci = (uint32_t)(row0 + (uint64_t)(c0 + j));
-#pragma unroll
-          for (int m = 0; m < KT; ++m) {
-            const bool sw = cd < kd[m] || (cd == kd[m] && ci < ki[m]);
-            const float td = kd[m];
-            const uint32_t ti = ki[m];
-            kd[m] = sw ? cd : td;
-            ki[m] = sw ? ci : ti;
-            cd = sw ? td : cd;
-            ci = sw ? ti : ci;
-          }
-#pragma unroll
-          for (int m = 0; m < KT; ++m) thr = (uint32_t)m == p.k - 1 ? kd[m] : thr;
-        }
-      }
+      // the next tile's norms into L1 while this one is scanned (two 128-byte lines per half)
+      if (lane < 2 && t + 1 < ntiles)
+        asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p.xn + row0 + kBN + half * kHalf + 32 * lane));
+      uint32_t va[32], vb[32];
+      tmem_ld32(tmem + lane_base + (uint32_t)(b * kBN + half * kHalf), va);
+      // second chunk requested now, waited for after the first chunk's work
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+          "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+          : "=r"(vb[0]), "=r"(vb[1]), "=r"(vb[2]), "=r"(vb[3]), "=r"(vb[4]), "=r"(vb[5]), "=r"(vb[6]), "=r"(vb[7]),
+            "=r"(vb[8]), "=r"(vb[9]), "=r"(vb[10]), "=r"(vb[11]), "=r"(vb[12]), "=r"(vb[13]), "=r"(vb[14]),
+            "=r"(vb[15]), "=r"(vb[16]), "=r"(vb[17]), "=r"(vb[18]), "=r"(vb[19]), "=r"(vb[20]), "=r"(vb[21]),
+            "=r"(vb[22]), "=r"(vb[23]), "=r"(vb[24]), "=r"(vb[25]), "=r"(vb[26]), "=r"(vb[27]), "=r"(vb[28]),
+            "=r"(vb[29]), "=r"(vb[30]), "=r"(vb[31])
+          : "r"(tmem + lane_base + (uint32_t)(b * kBN + half * kHalf + 32)));
+      scan_chunk<KT>(va, p.xn + row0 + half * kHalf, qnorm, (uint32_t)(row0 + half * kHalf), p.k, kd, ki, thr);
+      asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+      scan_chunk<KT>(vb, p.xn + row0 + half * kHalf + 32, qnorm, (uint32_t)(row0 + half * kHalf + 32), p.k, kd, ki, thr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(b));
     }
     if (qi < p.nq) {
-      const size_t o = ((size_t)sp * p.nq + qi) * p.k;
+      const size_t o = (((size_t)sp * 2 + (size_t)half) * p.nq + qi) * p.k;
 #pragma unroll
       for (int m = 0; m < KT; ++m)
         if ((uint32_t)m < p.k) {

@@ -1113,7 +1113,7 @@ int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint3
     uint64_t split_rows = (ix->n + splits - 1) / splits;
     split_rows = (split_rows + raven_tc::kBN - 1) / raven_tc::kBN * raven_tc::kBN;
     const uint64_t nsplit = (ix->n + split_rows - 1) / split_rows;
-    const size_t qbytes = nq_pad * kpad * 4, per = nsplit * nq * k;
+    const size_t qbytes = nq_pad * kpad * 4, per = 2 * nsplit * nq * k;  // two column halves per split
     const uint64_t n_pad = (ix->n + raven_tc::kBN - 1) / raven_tc::kBN * raven_tc::kBN;
     const size_t bytes = 2 * qbytes + nq_pad * 4 + n_pad * 4 + 16 + per * 8;
     uint8_t* tmp = nullptr;
@@ -1185,7 +1185,8 @@ int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint3
       }
     }
     if (e == cudaSuccess) {
-      knn_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(ti, td, (uint32_t)nsplit, nq, k, d_ids, d_dists);
+      knn_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(ti, td, (uint32_t)(2 * nsplit), nq, k, d_ids,
+                                                                          d_dists);
       e = cudaGetLastError();
     }
     int h_err = 0;
