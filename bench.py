@@ -60,6 +60,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=10000)
     ap.add_argument("--quant", choices=["sq4", "sq8"], default="sq4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the AdaptiveEf points and the 64-query latency run")
     ap.add_argument("--sweep", action="store_true", help="also report recall/QPS at other ef points")
     ap.add_argument("--hash-bits", type=int, default=0)
     return ap.parse_args()
@@ -252,7 +253,7 @@ def main():
 
     base, qbatches, g = load_workload(args, rank)
     quant = L.RAVEN_QUANT_SQ4 if args.quant == "sq4" else L.RAVEN_QUANT_SQ8
-    dev = DeviceIndex(g, base, device=dev_id, sq4=quant == 0, sq8=quant == 1, adaptive=False)
+    dev = DeviceIndex(g, base, device=dev_id, sq4=quant == 0, sq8=quant == 1, adaptive=True)
     if args.hash_bits:
         dev.set_tuning(hash_bits=args.hash_bits)
     lib = L.load()
@@ -402,6 +403,51 @@ def main():
         r50 = float(np.mean([len(set(g50[i]) & set(truth[i])) / k for i in range(g50.shape[0])]))
         ef50 = {"qps": nb * B / (e0.elapsed_time(e1) / 1e3), "recall_at_10": round(r50, 4)}
 
+    # AdaptiveEf Pareto points (gamma x (min_ef, max_ef)) on the same batches,
+    # and the small-batch latency run: 64-query launches, p50/p99 per launch
+    adaptive = latency = None
+    if rank == 0 and not args.no_extras:
+        adaptive = []
+        for gamma in (2.0, 2.4, 3.5):
+            for mn, mx in ((35, 65), (35, 75), (35, 85)):
+                pa = L.SearchParams(ef=mx, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=1,
+                                    gamma=gamma, min_ef=mn, max_ef=mx)
+                L.check(lib.raven_search_batch_device(dev._h, d_q[0].data_ptr(), B, C.byref(pa),
+                                                      C.byref(outs(0, with_stats=False)), stream.cuda_stream))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for r in range(nb):
+                    L.check(lib.raven_search_batch_device(dev._h, d_q[r].data_ptr(), B, C.byref(pa),
+                                                          C.byref(outs(r)), stream.cuda_stream))
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ga = d_ids.cpu().numpy().reshape(-1, k)
+                ra = float(np.mean([len(set(ga[i]) & set(truth[i])) / k for i in range(ga.shape[0])]))
+                adaptive.append({"gamma": gamma, "min_ef": mn, "max_ef": mx,
+                                 "qps": nb * B / (e0.elapsed_time(e1) / 1e3), "recall_at_10": round(ra, 4),
+                                 "mean_ef": float(stats["ef_used"].float().mean().item())})
+        lat_q, lat_n = 64, 300
+        ql = d_q[0][:lat_q]
+        lat = {}
+        for name, pl in (("ef%d" % args.ef, params),
+                         ("adaptive gamma=2.4 (35,75)", L.SearchParams(ef=75, k=k, rerank_factor=args.rr,
+                                                                        prefetch_offset=8, quant=quant, adaptive=1,
+                                                                        gamma=2.4, min_ef=35, max_ef=75))):
+            ol = outs(0, with_stats=False)
+            for _ in range(20):
+                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), lat_q, C.byref(pl), C.byref(ol),
+                                                      stream.cuda_stream))
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(lat_n)]
+            for a_, b_ in evs:
+                a_.record(stream)
+                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), lat_q, C.byref(pl), C.byref(ol),
+                                                      stream.cuda_stream))
+                b_.record(stream)
+            torch.cuda.synchronize()
+            ts = sorted(a_.elapsed_time(b_) * 1e3 for a_, b_ in evs)
+            lat[name] = {"p50_us": round(ts[len(ts) // 2], 1), "p99_us": round(ts[int(len(ts) * 0.99)], 1)}
+        latency = {"queries_per_launch": lat_q, "launches": lat_n, "device_time_per_launch": lat}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -444,6 +490,9 @@ def main():
     }
     if sweep is not None:
         line["config"]["ef_sweep"] = sweep
+    if adaptive is not None:
+        line["config"]["adaptive_ef"] = adaptive
+        line["config"]["latency_64q"] = latency
     if rank == 0:
         print(json.dumps(line), flush=True)
     del dev
