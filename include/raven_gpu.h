@@ -86,6 +86,19 @@ typedef struct {
 /* VamanaGraph::build (src/graph/vamana.rs:106-201) via PyIndex::build (src/python.rs:97-129). */
 RAVEN_API int raven_graph_build(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg,
                       raven_graph** out);
+
+/* Vamana build with the per-batch candidate step on a GPU (no reference
+ * counterpart on a GPU; replaces the search + prune loop of VamanaGraph::build,
+ * src/graph/vamana.rs:106-201). Same batches, random stream, connect step and
+ * final prune as raven_graph_build; each batch's nodes are searched by the
+ * engine's search kernel (entry = medoid, ef = l_build; the beam uses SQ4
+ * distances, so visited sets can differ slightly from an f32 search) and their
+ * visited sets pruned by DirectionalPrune on the GPU with f32 distances in the
+ * AVX-512 summation order. DirectionalPrune only (cfg->directional = 1);
+ * l_build <= 256, r_max <= 64, dim <= 256. The layered navigation is built on
+ * the host as in raven_graph_build. */
+RAVEN_API int raven_graph_build_gpu(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg,
+                                    int device, raven_graph** out);
 /* Serializable::load + VamanaGraph::deserialize (src/memory/serialize.rs:146, src/graph/vamana.rs:1326). */
 RAVEN_API int raven_graph_load(const char* path, raven_graph** out);
 RAVEN_API int raven_graph_load_bytes(const void* bytes, size_t len, raven_graph** out);

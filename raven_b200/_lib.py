@@ -108,6 +108,8 @@ class Limits(C.Structure):
 # name -> (restype, argtypes); every symbol declared in include/raven_gpu.h
 SIGNATURES = {
     "raven_graph_build": (C.c_int, [f32p, C.c_uint64, C.c_uint32, C.POINTER(BuildConfig), C.POINTER(C.c_void_p)]),
+    "raven_graph_build_gpu": (C.c_int, [f32p, C.c_uint64, C.c_uint32, C.POINTER(BuildConfig), C.c_int,
+                                        C.POINTER(C.c_void_p)]),
     "raven_graph_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
     "raven_graph_load_bytes": (C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]),
     "raven_graph_save": (C.c_int, [C.c_void_p, C.c_char_p]),

@@ -683,7 +683,8 @@ LayeredNav build_nav(const Ctx& c, uint64_t n, uint32_t entry, uint32_t m, uint3
 
 }  // namespace
 
-int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cfg, HostGraph* out, std::string* err) {
+int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cfg, HostGraph* out, std::string* err,
+                 BuildAccelerator* acc) {
   if (dim == 0 || cfg.r_max == 0 || cfg.l_build == 0 || cfg.r_max > 65535) {
     if (err) *err = "invalid build configuration";
     return -1;
@@ -716,6 +717,7 @@ int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cf
   }
   uint32_t entry = medoid(c, n);
   const size_t kBatch = 10000;
+  if (acc && n > 0 && acc->begin(g.mb.data(), n, g.r, entry, err) != 0) return -1;
   std::vector<Visit*> visits(threads, nullptr);
   std::vector<Pool> pools(threads);
   for (uint32_t iter = 0; iter < cfg.max_iterations && n > 0; ++iter) {
@@ -727,13 +729,21 @@ int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cf
     for (size_t b0 = 0; b0 < n; b0 += kBatch) {
       size_t b1 = std::min<size_t>(n, b0 + kBatch);
       std::vector<std::vector<uint32_t>> pruned(b1 - b0);
+      if (acc) {
+        if (acc->search_prune(order.data() + b0, b1 - b0, alpha, &pruned, err) != 0) {
+          for (Visit* v : visits) delete v;
+          return -1;
+        }
+      } else {
 #pragma omp parallel for schedule(dynamic, 16) num_threads(threads)
-      for (size_t p = b0; p < b1; ++p) {
-        int t = omp_get_thread_num();
-        if (!visits[t]) visits[t] = new Visit(n);
-        uint32_t node = order[p];
-        greedy_build(c, g, entry, c.vec(node), cfg.l_build, *visits[t], pools[t]);
-        pruned[p - b0] = prune_dispatch(c, cfg, visits[t]->hist, node, alpha, cfg.r_max, cfg.saturate && alpha > 1.0f);
+        for (size_t p = b0; p < b1; ++p) {
+          int t = omp_get_thread_num();
+          if (!visits[t]) visits[t] = new Visit(n);
+          uint32_t node = order[p];
+          greedy_build(c, g, entry, c.vec(node), cfg.l_build, *visits[t], pools[t]);
+          pruned[p - b0] =
+              prune_dispatch(c, cfg, visits[t]->hist, node, alpha, cfg.r_max, cfg.saturate && alpha > 1.0f);
+        }
       }
       // connect_bidirectional (vamana.rs:1117-1145), grouped by target node.
       struct Op {
@@ -765,6 +775,16 @@ int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cf
                                                         cfg.saturate && alpha > 1.0f));
             }
           }
+        }
+      }
+      if (acc) {
+        // every target of this batch's operations may have a new main block
+        std::vector<uint32_t> changed;
+        changed.reserve(n_seg);
+        for (size_t s2 = 0; s2 < n_seg; ++s2) changed.push_back(ops[seg[s2]].target);
+        if (acc->update_rows(changed.data(), changed.size(), g.mb.data(), err) != 0) {
+          for (Visit* v : visits) delete v;
+          return -1;
         }
       }
       if (cfg.verbose && (b0 / kBatch) % 10 == 0)

@@ -62,8 +62,25 @@ uint32_t crc32_ieee(const uint8_t* p, size_t n, uint32_t crc = 0);
 int parse_annx(const uint8_t* bytes, size_t len, HostGraph* g, std::string* err);
 std::vector<uint8_t> serialize_annx(const HostGraph& g);
 
+// The per-batch candidate step of the Vamana build (greedy search of the
+// current graph from the entry, then DirectionalPrune of the visited set),
+// done elsewhere (the GPU). build_vamana keeps the batch order, the
+// connect step and the final prune; the accelerator sees every change to
+// the searched rows through update_rows.
+struct BuildAccelerator {
+  virtual ~BuildAccelerator() = default;
+  // Once, before the first batch: the graph's main blocks (n * r, SENTINEL
+  // padded) and the entry point.
+  virtual int begin(const uint32_t* main_block, uint64_t n, uint64_t r, uint32_t entry, std::string* err) = 0;
+  // For each node of the batch: the pruned neighbour list.
+  virtual int search_prune(const uint32_t* nodes, size_t count, float alpha,
+                           std::vector<std::vector<uint32_t>>* pruned, std::string* err) = 0;
+  // Rows whose main block changed in the connect step.
+  virtual int update_rows(const uint32_t* ids, size_t count, const uint32_t* main_block, std::string* err) = 0;
+};
+
 int build_vamana(const float* vectors, uint64_t n, uint32_t dim, const BuildConfig& cfg, HostGraph* out,
-                 std::string* err);
+                 std::string* err, BuildAccelerator* acc = nullptr);
 
 // SQ4Params::fit / SQ8Params::fit (src/quant/sq4.rs:46-77, src/quant/sq8.rs:41-75):
 // out = 5*dim floats (min, max, scale, inv_scale, neg_min_div). The min/max

@@ -1397,3 +1397,331 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Vamana build on the GPU (no reference counterpart on a GPU: it replaces the
+// per-batch candidate step of VamanaGraph::build, src/graph/vamana.rs:106-201).
+// Per batch: the search kernel (entry = medoid, L = l_build, visited history
+// recorded) gives each node's candidate set, build_prune_kernel applies
+// DirectionalPrune to it; the host build keeps the batch order, the connect
+// step and the final prune, and sends back every changed row.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kPruneThreads = 256;
+constexpr uint32_t kBuildHistCap = 16384;  // visited ids kept per node (the rest are dropped, and counted)
+
+// DirectionalPrune (src/graph/robust_prune.rs:280-385) of one node's visited
+// set, one CTA per node. d(q, c) and l2(a, c) are f32 squared L2 in the
+// AVX-512 summation order (hw_dist). Candidates (node itself excluded) are
+// sorted by (distance, id) with a bitonic sort in shared memory; then in that
+// order a candidate is kept when no kept neighbour a has l2(a, c) < d(q, c),
+// until r_max are kept; if fewer than r_min are kept, a second pass adds, in
+// order, candidates not yet kept with l2(a, c) != 0 and d(q, c) / l2(a, c) <=
+// backfill_alpha for every kept a.
+__global__ void __launch_bounds__(kPruneThreads) build_prune_kernel(
+    const float* __restrict__ vec, uint32_t dim, uint32_t C, uint32_t rem, const uint32_t* __restrict__ nodes,
+    const uint32_t* __restrict__ hist, const uint32_t* __restrict__ hist_len, uint32_t hcap, uint32_t sortn,
+    uint32_t r_max, uint32_t r_min, float backfill_alpha, uint32_t* __restrict__ out, uint32_t* __restrict__ out_len) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const uint32_t stride = (dim + 3u) & ~3u;                    // 16-byte aligned rows
+  unsigned long long* keys = (unsigned long long*)sm;          // sortn
+  const uint32_t bit_words = ((sortn / 32) + 3u) & ~3u;       // 16-byte multiple: later rows stay aligned
+  uint32_t* kept_bits = (uint32_t*)(keys + sortn);             // bit i: sorted candidate i kept
+  uint32_t* kept_id = kept_bits + bit_words;                   // r_max (+ pad)
+  float* rows = (float*)(kept_id + ((r_max + 3u) & ~3u));      // r_max kept rows, then the candidate row
+  float* crow = rows + (size_t)r_max * stride;
+  __shared__ int viol;
+  __shared__ uint32_t nk, ncand;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, h = lane >> 4, j = lane & 15;
+  const uint32_t b = blockIdx.x;
+  const uint32_t node = nodes[b];
+  const float* qrow = vec + (size_t)node * dim;
+  const uint32_t len = min(hist_len[b], hcap);
+  const uint32_t* hb = hist + (size_t)b * hcap;
+  if (tid == 0) {
+    nk = 0;
+    ncand = 0;
+  }
+  for (uint32_t i = tid; i < bit_words; i += kPruneThreads) kept_bits[i] = 0;
+  __syncthreads();
+  // 1. keys = (distance bits, id); the node itself and padding sort last
+  //    (distances are >= 0, so their bit patterns order like the values)
+  for (uint32_t i0 = 2u * warp; i0 < sortn; i0 += 2u * (kPruneThreads / 32)) {
+    const uint32_t i = i0 + h;
+    const bool in = i < len;
+    const uint32_t id = in ? hb[i] : node;
+    float d = 0.0f;
+    if (i0 < len) d = hw_dist(qrow, vec + (size_t)id * dim, C, rem, j);  // both half-warps take this branch
+    if (j == 0) {
+      const bool ok = in && id != node;
+      keys[i] = ok ? ((unsigned long long)__float_as_uint(d) << 32) | id : ~0ull;
+      if (ok) atomicAdd(&ncand, 1u);
+    }
+  }
+  __syncthreads();
+  // 2. bitonic sort, ascending
+  for (uint32_t k2 = 2; k2 <= sortn; k2 <<= 1)
+    for (uint32_t jj = k2 >> 1; jj > 0; jj >>= 1) {
+      for (uint32_t i = tid; i < sortn; i += kPruneThreads) {
+        const uint32_t ixj = i ^ jj;
+        if (ixj > i) {
+          const unsigned long long x = keys[i], y = keys[ixj];
+          if ((x > y) == ((i & k2) == 0)) {
+            keys[i] = y;
+            keys[ixj] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  // 3. greedy selection, then the backfill pass
+  const uint32_t nc = ncand;
+  for (int pass = 0; pass < 2; ++pass) {
+    const uint32_t target = pass == 0 ? r_max : r_min;
+    for (uint32_t i = 0; i < nc; ++i) {
+      if (nk >= target) break;
+      if (pass == 1 && (kept_bits[i >> 5] >> (i & 31)) & 1u) continue;
+      const unsigned long long key = keys[i];
+      const uint32_t cid = (uint32_t)key;
+      const float dq = __uint_as_float((uint32_t)(key >> 32));
+      for (uint32_t e = tid; e < dim; e += kPruneThreads) crow[e] = vec[(size_t)cid * dim + e];
+      if (tid == 0) viol = 0;
+      __syncthreads();
+      const uint32_t m = nk;
+      for (uint32_t a0 = 2u * warp; a0 < m; a0 += 2u * (kPruneThreads / 32)) {
+        const uint32_t a = min(a0 + h, m - 1);
+        const float d = hw_dist(rows + (size_t)a * stride, crow, C, rem, j);
+        if (j == 0 && a0 + h < m) {
+          const bool bad = pass == 0 ? d < dq : (d == 0.0f || __fdiv_rn(dq, d) > backfill_alpha);
+          if (bad) viol = 1;
+        }
+      }
+      __syncthreads();
+      if (!viol) {
+        for (uint32_t e = tid; e < dim; e += kPruneThreads) rows[(size_t)m * stride + e] = crow[e];
+        if (tid == 0) {
+          kept_id[m] = cid;
+          kept_bits[i >> 5] |= 1u << (i & 31);
+          nk = m + 1;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (uint32_t t = tid; t < nk; t += kPruneThreads) out[(size_t)b * r_max + t] = kept_id[t];
+  if (tid == 0) out_len[b] = nk;
+}
+
+__global__ void build_scatter_rows_kernel(const uint32_t* __restrict__ ids, const uint32_t* __restrict__ rows,
+                                          uint64_t count, uint32_t r, uint32_t r_pad, uint32_t* __restrict__ adj) {
+  const uint64_t total = count * r_pad;
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = t / r_pad;
+    const uint32_t c = (uint32_t)(t - i * r_pad);
+    adj[(uint64_t)ids[i] * r_pad + c] = c < r ? rows[i * r + c] : raven::kSentinel;
+  }
+}
+
+struct GpuBuild : raven::BuildAccelerator {
+  const float* h_vec;
+  uint64_t n;
+  uint32_t dim;
+  raven::BuildConfig cfg;
+  int device;
+  raven_index* ix = nullptr;
+  float* d_nat = nullptr;
+  uint8_t* d_buf = nullptr;
+  uint32_t *d_nodes = nullptr, *d_hist = nullptr, *d_hlen = nullptr, *d_ids = nullptr, *d_pruned = nullptr,
+           *d_plen = nullptr, *d_rows = nullptr;
+  float *d_q = nullptr, *d_dists = nullptr;
+  int32_t* d_status = nullptr;
+  size_t cap_nodes = 0, cap_rows = 0;
+  uint64_t truncated = 0;  // nodes whose visited set exceeded kBuildHistCap
+
+  GpuBuild(const float* v, uint64_t n_, uint32_t d, const raven::BuildConfig& c, int dev)
+      : h_vec(v), n(n_), dim(d), cfg(c), device(dev) {}
+  ~GpuBuild() override {
+    if (d_nat) cudaFree(d_nat);
+    if (d_buf) cudaFree(d_buf);
+    if (d_rows) cudaFree(d_rows);
+    if (ix) raven_index_free(ix);
+  }
+  static int cuda_err(cudaError_t e, std::string* err, const char* what) {
+    if (e == cudaSuccess) return 0;
+    if (err) *err = std::string(what) + ": " + cudaGetErrorString(e);
+    return RAVEN_ECUDA;
+  }
+  int begin(const uint32_t* main_block, uint64_t n_, uint64_t r, uint32_t entry, std::string* err) override {
+    raven_graph gr;
+    gr.g.n = n_;
+    gr.g.dim = dim;
+    gr.g.r_max = r;
+    gr.g.entry = entry;
+    gr.g.main_block.assign(main_block, main_block + n_ * r);
+    gr.g.degrees.resize(n_);
+    gr.g.overflow.resize(n_);
+    for (uint64_t v = 0; v < n_; ++v) {
+      uint16_t d = 0;
+      while (d < r && main_block[v * r + d] != raven::kSentinel) ++d;
+      gr.g.degrees[v] = d;
+    }
+    raven_upload_options o{device, 1, 0, 0};
+    int rc = raven_index_upload(&gr, h_vec, n_, dim, &o, &ix);
+    if (rc) {
+      if (err) *err = raven_last_error();
+      return rc;
+    }
+    if (int e = cuda_err(cudaMalloc((void**)&d_nat, n_ * dim * 4), err, "build: vectors")) return e;
+    return cuda_err(cudaMemcpy(d_nat, h_vec, n_ * dim * 4, cudaMemcpyHostToDevice), err, "build: vectors");
+  }
+  int ensure(size_t count, std::string* err) {
+    if (count <= cap_nodes) return 0;
+    if (d_buf) cudaFree(d_buf);
+    d_buf = nullptr;
+    const size_t per = 4 * (1 + kBuildHistCap + 1 + 1 + cfg.r_max + 1 + 1) + 4 * (size_t)dim + 4;
+    if (int e = cuda_err(cudaMalloc((void**)&d_buf, count * per + 256), err, "build: batch buffers")) return e;
+    uint8_t* p = d_buf;
+    auto take = [&](size_t bytes) { uint8_t* q = p; p += (bytes + 15) & ~(size_t)15; return q; };
+    d_nodes = (uint32_t*)take(count * 4);
+    d_hist = (uint32_t*)take(count * kBuildHistCap * 4);
+    d_hlen = (uint32_t*)take(count * 4);
+    d_ids = (uint32_t*)take(count * 4);
+    d_pruned = (uint32_t*)take(count * cfg.r_max * 4);
+    d_plen = (uint32_t*)take(count * 4);
+    d_status = (int32_t*)take(count * 4);
+    d_q = (float*)take(count * dim * 4);
+    d_dists = (float*)take(count * 4);
+    cap_nodes = count;
+    return 0;
+  }
+  int search_prune(const uint32_t* nodes, size_t count, float alpha, std::vector<std::vector<uint32_t>>* pruned,
+                   std::string* err) override {
+    if (int e = ensure(count, err)) return e;
+    cudaStream_t st = ix->stream;
+    if (int e = cuda_err(cudaMemcpyAsync(d_nodes, nodes, count * 4, cudaMemcpyHostToDevice, st), err, "build: ids"))
+      return e;
+    gather_rows_kernel<<<ix->num_sms * 4, 256, 0, st>>>(d_nat, d_nodes, count, dim, d_q);
+    raven_search_params p{};
+    p.ef = cfg.l_build;
+    p.k = 1;
+    p.rerank_factor = 1;
+    p.quant = RAVEN_QUANT_SQ4;
+    raven_search_outputs o{};
+    o.ids = d_ids;
+    o.dists = d_dists;
+    o.status = d_status;
+    o.history = d_hist;
+    o.history_cap = kBuildHistCap;
+    o.history_len = d_hlen;
+    int rc = raven_search_batch_device(ix, d_q, count, &p, &o, st);
+    if (rc) {
+      if (err) *err = raven_last_error();
+      return rc;
+    }
+    std::vector<uint32_t> hlen(count);
+    if (int e = cuda_err(cudaMemcpyAsync(hlen.data(), d_hlen, count * 4, cudaMemcpyDeviceToHost, st), err,
+                         "build: history lengths"))
+      return e;
+    if (int e = cuda_err(cudaStreamSynchronize(st), err, "build: search")) return e;
+    uint32_t mx = 32;
+    for (uint32_t v : hlen) {
+      mx = std::max(mx, std::min(v, kBuildHistCap));
+      if (v > kBuildHistCap) ++truncated;
+    }
+    uint32_t sortn = 32;
+    while (sortn < mx) sortn <<= 1;
+    const uint32_t stride = (dim + 3u) & ~3u;
+    const size_t bit_words = ((sortn / 32) + 3u) & ~3u;
+    const size_t smem =
+        (size_t)sortn * 8 + bit_words * 4 + ((cfg.r_max + 3u) & ~3u) * 4 + (size_t)(cfg.r_max + 1) * stride * 4;
+    if (smem > 227 * 1024) {
+      if (err) *err = "build: prune workspace above the shared-memory limit";
+      return RAVEN_ELIMIT;
+    }
+    const uint32_t div = cfg.rmin_divisor ? cfg.rmin_divisor : 4;
+    const uint32_t r_min = std::max<uint32_t>(cfg.r_max / div, 1);
+    const float bf_alpha = std::max(alpha, 1.0f);
+    cudaFuncSetAttribute(build_prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    build_prune_kernel<<<(unsigned)count, kPruneThreads, smem, st>>>(ix->d_vec, dim, dim / 16, dim % 16, d_nodes,
+                                                                      d_hist, d_hlen, kBuildHistCap, sortn, cfg.r_max,
+                                                                      r_min, bf_alpha, d_pruned, d_plen);
+    if (int e = cuda_err(cudaGetLastError(), err, "build: prune")) return e;
+    std::vector<uint32_t> pr(count * cfg.r_max), pl(count);
+    cudaMemcpyAsync(pr.data(), d_pruned, pr.size() * 4, cudaMemcpyDeviceToHost, st);
+    cudaMemcpyAsync(pl.data(), d_plen, count * 4, cudaMemcpyDeviceToHost, st);
+    if (int e = cuda_err(cudaStreamSynchronize(st), err, "build: prune")) return e;
+    for (size_t i = 0; i < count; ++i)
+      (*pruned)[i].assign(pr.begin() + i * cfg.r_max, pr.begin() + i * cfg.r_max + pl[i]);
+    return 0;
+  }
+  int update_rows(const uint32_t* ids, size_t count, const uint32_t* main_block, std::string* err) override {
+    if (count == 0) return 0;
+    const uint32_t r = cfg.r_max;
+    if (count > cap_rows) {
+      if (d_rows) cudaFree(d_rows);
+      d_rows = nullptr;
+      if (int e = cuda_err(cudaMalloc((void**)&d_rows, count * (r + 1) * 4), err, "build: row staging")) return e;
+      cap_rows = count;
+    }
+    std::vector<uint32_t> stage(count * (size_t)(r + 1));
+    uint32_t* sid = stage.data();
+    uint32_t* srow = stage.data() + count;
+    for (size_t i = 0; i < count; ++i) {
+      sid[i] = ids[i];
+      std::memcpy(srow + i * r, main_block + (size_t)ids[i] * r, r * 4);
+    }
+    cudaStream_t st = ix->stream;
+    if (int e = cuda_err(cudaMemcpyAsync(d_rows, stage.data(), stage.size() * 4, cudaMemcpyHostToDevice, st), err,
+                         "build: rows"))
+      return e;
+    build_scatter_rows_kernel<<<ix->num_sms * 4, 256, 0, st>>>(d_rows, d_rows + count, count, r, ix->r_pad, ix->d_adj);
+    return cuda_err(cudaStreamSynchronize(st), err, "build: rows");
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int raven_graph_build_gpu(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg, int device,
+                          raven_graph** out) {
+  if (!out || (!vectors && n) || !cfg) return fail(RAVEN_EINVAL, "null argument");
+  raven::BuildConfig c;
+  c.alpha = cfg->alpha;
+  c.l_build = cfg->l_build;
+  c.r_max = cfg->r_max;
+  c.r_soft = cfg->r_soft;
+  c.max_iterations = cfg->max_iterations;
+  c.saturate = cfg->saturate != 0;
+  c.enable_layered_nav = cfg->layered_nav != 0;
+  c.nav_m = cfg->nav_m;
+  c.directional = cfg->directional != 0;
+  c.seed = cfg->seed;
+  c.threads = cfg->threads;
+  c.verbose = cfg->verbose;
+  if (c.nav_m < 2) return fail(RAVEN_EINVAL, "nav_m must be >= 2");
+  if (!c.directional) return fail(RAVEN_EINVAL, "the GPU build implements DirectionalPrune (directional=1)");
+  if (c.l_build == 0 || c.l_build > kMaxEf) return fail(RAVEN_ELIMIT, "l_build must be in 1..256 for the GPU build");
+  if (c.r_max == 0 || c.r_max > 64) return fail(RAVEN_ELIMIT, "r_max must be in 1..64 for the GPU build");
+  if (dim == 0 || dim > kMaxDimSq4) return fail(RAVEN_ELIMIT, "dim must be in 1..256 for the GPU build");
+  if (n < 2) return fail(RAVEN_EINVAL, "the GPU build needs at least 2 vectors");
+  raven_graph* g = new raven_graph();
+  std::string err;
+  int rc;
+  {
+    GpuBuild acc(vectors, n, dim, c, device);
+    rc = raven::build_vamana(vectors, n, dim, c, &g->g, &err, &acc);
+    if (!rc && acc.truncated && c.verbose)
+      fprintf(stderr, "[build] %llu nodes had more than %u visited ids (first ones kept)\n",
+              (unsigned long long)acc.truncated, kBuildHistCap);
+  }
+  if (rc) {
+    delete g;
+    return fail(rc < 0 ? RAVEN_ECUDA : rc, err);
+  }
+  *out = g;
+  return RAVEN_OK;
+}
+
+}  // extern "C"

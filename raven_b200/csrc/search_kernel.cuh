@@ -218,7 +218,9 @@ __device__ inline float hw_dist(const float* __restrict__ qf, const float* __res
   const float* q = qf + j * C;
   const float* r = row + j * C;
   uint32_t c = 0;
-  if ((C & 3u) == 0) {
+  // 16-byte loads only when both rows are 16-byte aligned (a staged row of a
+  // dim that is not a multiple of 4 is not); same summation order either way
+  if ((C & 3u) == 0 && (((uintptr_t)q | (uintptr_t)r) & 15u) == 0) {
     for (; c < C; c += 4) {
       const float4 qa = *(const float4*)(q + c);
       const float4 ra = *(const float4*)(r + c);

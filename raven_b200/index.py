@@ -39,8 +39,12 @@ class Graph:
     @classmethod
     def build(cls, vectors, r: int = 32, l: int = 200, alpha: float = 1.2, nav_m: int = 32,
               directional: bool = True, r_soft: Optional[int] = None, max_iterations: int = 2,
-              seed: int = 42, threads: int = 0, layered_nav: bool = True, verbose: bool = False) -> "Graph":
-        """VamanaGraph::build with the PyO3 configuration (src/python.rs:109-126)."""
+              seed: int = 42, threads: int = 0, layered_nav: bool = True, verbose: bool = False,
+              device: Optional[int] = None) -> "Graph":
+        """VamanaGraph::build with the PyO3 configuration (src/python.rs:109-126).
+
+        `device`: run each batch's search + DirectionalPrune on that GPU
+        (raven_graph_build_gpu); None builds on the host."""
         lib = L.load()
         v = _f32c(vectors)
         if v.ndim != 2:
@@ -52,7 +56,11 @@ class Graph:
             nav_m=nav_m, directional=1 if directional else 0, seed=seed, threads=threads, verbose=1 if verbose else 0,
         )
         h = C.c_void_p()
-        L.check(lib.raven_graph_build(L.ptr(v, C.c_float), v.shape[0], v.shape[1], C.byref(cfg), C.byref(h)))
+        if device is None:
+            L.check(lib.raven_graph_build(L.ptr(v, C.c_float), v.shape[0], v.shape[1], C.byref(cfg), C.byref(h)))
+        else:
+            L.check(lib.raven_graph_build_gpu(L.ptr(v, C.c_float), v.shape[0], v.shape[1], C.byref(cfg), int(device),
+                                              C.byref(h)))
         return cls(h.value)
 
     @classmethod

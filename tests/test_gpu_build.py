@@ -1,0 +1,77 @@
+"""Vamana build with the per-batch search + DirectionalPrune on the GPU
+(raven_graph_build_gpu): a valid graph (degrees within r_max, no self loops,
+no repeated neighbours, ids in range, navigation built), deterministic (two
+builds serialise to the same bytes), searchable with oracle parity, and of
+the same quality as the host build (recall@10 at ef=50 within 0.02).
+"""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def data(raven_lib):
+    from raven_b200 import datasets
+
+    base = datasets.clustered_int(20000, 128, 200, 12.0, seed=11, centre_seed=12)
+    q = datasets.clustered_int(500, 128, 200, 12.0, seed=13, centre_seed=12)
+    return base, q
+
+
+def _build(base, device):
+    from raven_b200.index import Graph
+
+    return Graph.build(base, r=32, l=100, alpha=1.2, nav_m=16, directional=True, seed=5, device=device)
+
+
+def _bytes(g):
+    with tempfile.TemporaryDirectory() as d:
+        p = os.path.join(d, "g.annx")
+        g.save(p)
+        return open(p, "rb").read()
+
+
+def test_gpu_build_structure_and_determinism(data):
+    base, _ = data
+    g1 = _build(base, 0)
+    n = base.shape[0]
+    info = g1.info()
+    assert info.n == n and info.r_max == 32 and info.has_nav
+    for v in range(0, n, 97):
+        nb = g1.neighbors(v)
+        assert len(nb) <= 32
+        assert v not in set(nb.tolist())
+        assert len(set(nb.tolist())) == len(nb)
+        assert np.all(nb < n)
+    assert _bytes(g1) == _bytes(_build(base, 0))
+
+
+def test_gpu_build_search_parity_and_quality(data, oracle):
+    from raven_b200 import _lib as L
+    from raven_b200.index import DeviceIndex
+
+    base, q = data
+    gi, _ = oracle.bruteforce(base, q, 10)
+    recalls = {}
+    for name, dev_id in (("gpu", 0), ("host", None)):
+        g = _build(base, dev_id)
+        dev = DeviceIndex(g, base, sq4=True)
+        p = L.SearchParams(ef=50, k=10, rerank_factor=8, prefetch_offset=8, quant=0, adaptive=0, gamma=0.0, min_ef=0,
+                           max_ef=0)
+        got = dev.search(q, p)
+        assert np.all(got["status"] == 0)
+        recalls[name] = np.mean([len(set(got["ids"][i]) & set(gi[i])) / 10 for i in range(q.shape[0])])
+        if name == "gpu":
+            with tempfile.TemporaryDirectory() as d:
+                path = os.path.join(d, "g.annx")
+                g.save(path)
+                oi = oracle.OracleIndex(path)
+            oi.set_vectors(base, sq4=True)
+            exp = oi.search(q, k=10, ef=50, rerank_factor=8)
+            np.testing.assert_array_equal(got["ids"], exp["ids"])
+            np.testing.assert_array_equal(got["visited"], exp["visited"])
+    assert recalls["gpu"] >= recalls["host"] - 0.02, recalls

@@ -397,3 +397,22 @@ def test_gmm1m_headline_parity(oracle, raven_lib):
         got = dev.search(q[:2000], _params(ef=ef), history_cap=8192)
         exp = oi.search(q[:2000], k=10, ef=ef, rerank_factor=8, history_cap=8192)
         _compare(got, exp)
+
+
+@pytest.mark.parametrize("dim", [70, 131])
+def test_odd_dim_parity(oracle, raven_lib, dim):
+    """Dims whose 16-lane chains are a multiple of 4 long but whose rows are not
+    a multiple of 4 floats: staged rows are then not 16-byte aligned (scalar
+    loads), descent, search and rerank must still match the oracle."""
+    from raven_b200 import datasets
+    from raven_b200.index import DeviceIndex, Graph
+
+    base = datasets.clustered_int(3000, dim, 30, 12.0, seed=dim, centre_seed=dim + 1)
+    q = datasets.clustered_int(200, dim, 30, 12.0, seed=dim + 2, centre_seed=dim + 1)
+    g = Graph.build(base, r=32, l=64, alpha=1.2, nav_m=8, directional=True, seed=3)
+    dev = DeviceIndex(g, base, sq4=True, sq8=dim <= 128, adaptive=True)
+    oi = _oracle_for(oracle, g, base, sq8=dim <= 128)
+    for quant in ([0, 1] if dim <= 128 else [0]):
+        got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, quant=quant), history_cap=4096)
+        exp = oi.search(q, k=10, ef=50, rerank_factor=8, quant=quant, history_cap=4096)
+        _compare(got, exp)
