@@ -815,7 +815,9 @@ int build_vamana(const float* V, uint64_t n, uint32_t dim, const BuildConfig& cf
            cfg.r_soft);
   out->metadata_toml = meta;
   if (cfg.enable_layered_nav && n > 0) {
+    const double t_nav = omp_get_wtime();
     out->nav = build_nav(c, n, entry, cfg.nav_m, cfg.r_max / 2, cfg.verbose);
+    if (cfg.verbose) fprintf(stderr, "[nav] built in %.1f s\n", omp_get_wtime() - t_nav);
   } else {
     out->nav = LayeredNav();
   }

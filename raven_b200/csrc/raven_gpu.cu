@@ -13,6 +13,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -1429,7 +1430,7 @@ __global__ void __launch_bounds__(kPruneThreads) build_prune_kernel(
   const uint32_t bit_words = ((sortn / 32) + 3u) & ~3u;       // 16-byte multiple: later rows stay aligned
   uint32_t* kept_bits = (uint32_t*)(keys + sortn);             // bit i: sorted candidate i kept
   uint32_t* kept_id = kept_bits + bit_words;                   // r_max (+ pad)
-  float* rows = (float*)(kept_id + ((r_max + 3u) & ~3u));      // r_max kept rows, then the candidate row
+  float* rows = (float*)(kept_id + ((r_max + 3u) & ~3u));      // r_max kept rows, then 16 candidate rows
   float* crow = rows + (size_t)r_max * stride;
   __shared__ int viol;
   __shared__ uint32_t nk, ncand;
@@ -1475,36 +1476,71 @@ __global__ void __launch_bounds__(kPruneThreads) build_prune_kernel(
       }
       __syncthreads();
     }
-  // 3. greedy selection, then the backfill pass
+  // 3. greedy selection, then the backfill pass, 16 candidates at a time:
+  //    each half-warp tests one candidate against every row kept before the
+  //    chunk, then warp 0 walks the chunk in order and tests the survivors
+  //    against the candidates it accepted earlier in the same chunk, which
+  //    gives the decisions of the one-at-a-time loop.
   const uint32_t nc = ncand;
+  constexpr int kChunk = 2 * (kPruneThreads / 32);
+  __shared__ uint32_t cidx[kChunk];
+  __shared__ int cviol[kChunk];
+  __shared__ uint32_t cn, next_i;
+  if (tid == 0) next_i = 0;
   for (int pass = 0; pass < 2; ++pass) {
     const uint32_t target = pass == 0 ? r_max : r_min;
-    for (uint32_t i = 0; i < nc; ++i) {
-      if (nk >= target) break;
-      if (pass == 1 && (kept_bits[i >> 5] >> (i & 31)) & 1u) continue;
-      const unsigned long long key = keys[i];
-      const uint32_t cid = (uint32_t)key;
-      const float dq = __uint_as_float((uint32_t)(key >> 32));
-      for (uint32_t e = tid; e < dim; e += kPruneThreads) crow[e] = vec[(size_t)cid * dim + e];
-      if (tid == 0) viol = 0;
-      __syncthreads();
-      const uint32_t m = nk;
-      for (uint32_t a0 = 2u * warp; a0 < m; a0 += 2u * (kPruneThreads / 32)) {
-        const uint32_t a = min(a0 + h, m - 1);
-        const float d = hw_dist(rows + (size_t)a * stride, crow, C, rem, j);
-        if (j == 0 && a0 + h < m) {
-          const bool bad = pass == 0 ? d < dq : (d == 0.0f || __fdiv_rn(dq, d) > backfill_alpha);
-          if (bad) viol = 1;
-        }
+    if (tid == 0) next_i = 0;
+    __syncthreads();
+    while (true) {
+      if (tid == 0) {
+        uint32_t c = 0, i = next_i;
+        for (; i < nc && c < (uint32_t)kChunk; ++i)
+          if (pass == 0 || !((kept_bits[i >> 5] >> (i & 31)) & 1u)) cidx[c++] = i;
+        cn = c;
+        next_i = i;
       }
       __syncthreads();
-      if (!viol) {
-        for (uint32_t e = tid; e < dim; e += kPruneThreads) rows[(size_t)m * stride + e] = crow[e];
-        if (tid == 0) {
-          kept_id[m] = cid;
-          kept_bits[i >> 5] |= 1u << (i & 31);
-          nk = m + 1;
+      const uint32_t m = nk, n_chunk = cn;
+      if (n_chunk == 0 || m >= target) break;
+      // stage the chunk's rows after the kept rows
+      for (uint32_t e = tid; e < n_chunk * dim; e += kPruneThreads) {
+        const uint32_t t = e / dim, d = e - t * dim;
+        crow[t * stride + d] = vec[(size_t)(uint32_t)keys[cidx[t]] * dim + d];
+      }
+      __syncthreads();
+      {
+        const uint32_t t = 2u * warp + h;  // this half-warp's candidate
+        const uint32_t tt = min(t, n_chunk - 1);
+        const float dq = __uint_as_float((uint32_t)(keys[cidx[tt]] >> 32));
+        bool bad = false;
+        for (uint32_t a = 0; a < m; ++a) {
+          if (__all_sync(kFull, bad)) break;  // both half-warps decided (the distance needs the whole warp)
+          const float d = hw_dist(rows + (size_t)a * stride, crow + (size_t)tt * stride, C, rem, j);
+          bad |= pass == 0 ? d < dq : (d == 0.0f || __fdiv_rn(dq, d) > backfill_alpha);
         }
+        if (j == 0 && t < n_chunk) cviol[t] = bad ? 1 : 0;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        uint32_t first_new = m, cnt = m;
+        for (uint32_t t = 0; t < n_chunk && cnt < target; ++t) {
+          if (cviol[t]) continue;
+          const float dq = __uint_as_float((uint32_t)(keys[cidx[t]] >> 32));
+          bool bad = false;
+          for (uint32_t s2 = first_new; s2 < cnt && !bad; ++s2) {
+            const float d = hw_dist(rows + (size_t)s2 * stride, crow + (size_t)t * stride, C, rem, j);
+            bad = pass == 0 ? d < dq : (d == 0.0f || __fdiv_rn(dq, d) > backfill_alpha);
+          }
+          if (bad) continue;
+          for (uint32_t e = lane; e < dim; e += 32) rows[(size_t)cnt * stride + e] = crow[(size_t)t * stride + e];
+          if (lane == 0) {
+            kept_id[cnt] = (uint32_t)keys[cidx[t]];
+            kept_bits[cidx[t] >> 5] |= 1u << (cidx[t] & 31);
+          }
+          __syncwarp();
+          ++cnt;
+        }
+        if (lane == 0) nk = cnt;
       }
       __syncthreads();
     }
@@ -1538,6 +1574,10 @@ struct GpuBuild : raven::BuildAccelerator {
   int32_t* d_status = nullptr;
   size_t cap_nodes = 0, cap_rows = 0;
   uint64_t truncated = 0;  // nodes whose visited set exceeded kBuildHistCap
+  double t_search = 0, t_prune = 0, t_rows = 0;  // seconds, reported in verbose builds
+  static double now() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+  }
 
   GpuBuild(const float* v, uint64_t n_, uint32_t d, const raven::BuildConfig& c, int dev)
       : h_vec(v), n(n_), dim(d), cfg(c), device(dev) {}
@@ -1598,6 +1638,7 @@ struct GpuBuild : raven::BuildAccelerator {
   int search_prune(const uint32_t* nodes, size_t count, float alpha, std::vector<std::vector<uint32_t>>* pruned,
                    std::string* err) override {
     if (int e = ensure(count, err)) return e;
+    const double t0 = now();
     cudaStream_t st = ix->stream;
     if (int e = cuda_err(cudaMemcpyAsync(d_nodes, nodes, count * 4, cudaMemcpyHostToDevice, st), err, "build: ids"))
       return e;
@@ -1624,6 +1665,8 @@ struct GpuBuild : raven::BuildAccelerator {
                          "build: history lengths"))
       return e;
     if (int e = cuda_err(cudaStreamSynchronize(st), err, "build: search")) return e;
+    const double t1 = now();
+    t_search += t1 - t0;
     uint32_t mx = 32;
     for (uint32_t v : hlen) {
       mx = std::max(mx, std::min(v, kBuildHistCap));
@@ -1633,8 +1676,8 @@ struct GpuBuild : raven::BuildAccelerator {
     while (sortn < mx) sortn <<= 1;
     const uint32_t stride = (dim + 3u) & ~3u;
     const size_t bit_words = ((sortn / 32) + 3u) & ~3u;
-    const size_t smem =
-        (size_t)sortn * 8 + bit_words * 4 + ((cfg.r_max + 3u) & ~3u) * 4 + (size_t)(cfg.r_max + 1) * stride * 4;
+    const size_t smem = (size_t)sortn * 8 + bit_words * 4 + ((cfg.r_max + 3u) & ~3u) * 4 +
+                        (size_t)(cfg.r_max + 2 * (kPruneThreads / 32)) * stride * 4;
     if (smem > 227 * 1024) {
       if (err) *err = "build: prune workspace above the shared-memory limit";
       return RAVEN_ELIMIT;
@@ -1653,10 +1696,12 @@ struct GpuBuild : raven::BuildAccelerator {
     if (int e = cuda_err(cudaStreamSynchronize(st), err, "build: prune")) return e;
     for (size_t i = 0; i < count; ++i)
       (*pruned)[i].assign(pr.begin() + i * cfg.r_max, pr.begin() + i * cfg.r_max + pl[i]);
+    t_prune += now() - t1;
     return 0;
   }
   int update_rows(const uint32_t* ids, size_t count, const uint32_t* main_block, std::string* err) override {
     if (count == 0) return 0;
+    const double t0 = now();
     const uint32_t r = cfg.r_max;
     if (count > cap_rows) {
       if (d_rows) cudaFree(d_rows);
@@ -1676,7 +1721,9 @@ struct GpuBuild : raven::BuildAccelerator {
                          "build: rows"))
       return e;
     build_scatter_rows_kernel<<<ix->num_sms * 4, 256, 0, st>>>(d_rows, d_rows + count, count, r, ix->r_pad, ix->d_adj);
-    return cuda_err(cudaStreamSynchronize(st), err, "build: rows");
+    const int e = cuda_err(cudaStreamSynchronize(st), err, "build: rows");
+    t_rows += now() - t0;
+    return e;
   }
 };
 
@@ -1711,7 +1758,12 @@ int raven_graph_build_gpu(const float* vectors, uint64_t n, uint32_t dim, const 
   int rc;
   {
     GpuBuild acc(vectors, n, dim, c, device);
+    const double t0 = GpuBuild::now();
     rc = raven::build_vamana(vectors, n, dim, c, &g->g, &err, &acc);
+    if (!rc && c.verbose)
+      fprintf(stderr, "[build] total %.1f s: GPU search %.1f s, GPU prune %.1f s, row updates %.1f s, host rest %.1f s\n",
+              GpuBuild::now() - t0, acc.t_search, acc.t_prune, acc.t_rows,
+              GpuBuild::now() - t0 - acc.t_search - acc.t_prune - acc.t_rows);
     if (!rc && acc.truncated && c.verbose)
       fprintf(stderr, "[build] %llu nodes had more than %u visited ids (first ones kept)\n",
               (unsigned long long)acc.truncated, kBuildHistCap);

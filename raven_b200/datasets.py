@@ -119,8 +119,10 @@ def index_path(name: str, n: int | None = None) -> str:
     return _os.path.join(DATA_DIR, f"{name}-n{n}.annx")
 
 
-def load_or_build(name: str, base=None, n: int | None = None, threads: int = 0, verbose: bool = False):
-    """Load the cached graph for a workload or build and save it."""
+def load_or_build(name: str, base=None, n: int | None = None, threads: int = 0, verbose: bool = False,
+                  device: int | None = None):
+    """Load the cached graph for a workload or build and save it (on the host,
+    or with the GPU candidate step when `device` is given)."""
     from .index import Graph
 
     path = index_path(name, n)
@@ -128,7 +130,8 @@ def load_or_build(name: str, base=None, n: int | None = None, threads: int = 0, 
         return Graph.load(path)
     if base is None:
         base, _ = make(name, n=n, nq=1)
-    g = Graph.build(base, r=32, l=200, alpha=1.2, nav_m=32, directional=True, threads=threads, verbose=verbose)
+    g = Graph.build(base, r=32, l=200, alpha=1.2, nav_m=32, directional=True, threads=threads, verbose=verbose,
+                    device=device)
     _os.makedirs(DATA_DIR, exist_ok=True)
     tmp = path + ".tmp"
     g.save(tmp)
