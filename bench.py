@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the AdaptiveEf points and the 64-query latency run")
     ap.add_argument("--sweep", action="store_true", help="also report recall/QPS at other ef points")
     ap.add_argument("--hash-bits", type=int, default=0)
+    ap.add_argument("--shards", type=int, default=0,
+                    help="split the workload into this many per-shard graphs (all-gather + merge across ranks)")
+    ap.add_argument("--shard-n", type=int, default=0, help="vectors per shard (default: workload n / shards)")
     ap.add_argument("--build-device", type=int, default=None,
                     help="build a missing index with the GPU candidate step on this device (default: host build)")
     return ap.parse_args()
@@ -230,10 +233,160 @@ def run_reference(args):
     return 0
 
 
+def run_sharded(args):
+    """Collection split into `args.shards` contiguous per-shard graphs (shard s
+    on rank s % world): every query is searched on every shard, the per-shard
+    top-k lists are all-gathered and merged on the GPU (raven_b200.multigpu).
+    A step = one batch through ShardedCollection.search; recall against the
+    exact kNN of the whole collection (exact per shard, merged the same way)."""
+    import datetime
+
+    import torch
+    import torch.distributed as tdist
+
+    from raven_b200 import _lib as L
+    from raven_b200 import datasets
+    from raven_b200 import multigpu as M
+    from raven_b200.index import DeviceIndex, Graph
+
+    rank, world, local = dist_env()
+    dist = world > 1
+    torch.cuda.set_device(local)
+    if dist:
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800),
+                                 device_id=torch.device("cuda", local))
+    S = args.shards
+    shard_n = args.shard_n or datasets.WORKLOADS[args.workload]["n"] // S
+    mine = M.shards_of_rank(S, world, rank)
+    t0 = time.time()
+    shards = {}
+    for sh in mine:
+        base = datasets.make_shard(args.workload, sh, S, shard_n)
+        path = datasets.shard_index_path(args.workload, sh, S, shard_n)
+        if os.path.exists(path):
+            g = Graph.load(path)
+        else:
+            g = Graph.build(base, r=32, l=200, alpha=1.2, nav_m=32, directional=True, seed=42 + sh,
+                            device=local if args.build_device is not None else None)
+            os.makedirs(os.path.dirname(path), exist_ok=True)
+            g.save(path + ".tmp")
+            os.replace(path + ".tmp", path)
+        shards[sh] = DeviceIndex(g, base, device=local, sq4=True)
+        del base
+    build_s = time.time() - t0
+    lib = L.load()
+    coll = M.ShardedCollection(shards, S, shard_n)
+    B, k = args.batch, args.k
+    qb = np.stack([datasets.make_queries(args.workload, B, offset=b) for b in range(N_BATCHES)])
+    d_q = torch.from_numpy(qb).cuda()
+    params = L.SearchParams(ef=args.ef, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=L.RAVEN_QUANT_SQ4,
+                            adaptive=0, gamma=0.0, min_ef=0, max_ef=0)
+    stream = torch.cuda.Stream()
+    # exact kNN of the whole collection: exact per local shard, exchanged and merged
+    truth = []
+    for b in range(N_BATCHES):
+        gi = torch.zeros((len(mine), B, k), dtype=torch.int32, device="cuda")
+        gd = torch.zeros((len(mine), B, k), dtype=torch.float32, device="cuda")
+        for j, sh in enumerate(mine):
+            L.check(lib.raven_knn_exact_device(shards[sh]._h, d_q[b].data_ptr(), B, k, gi[j].data_ptr(),
+                                               gd[j].data_ptr(), stream.cuda_stream))
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            packed = M.pack_lists(gi, gd, torch.full((len(mine), B), k, dtype=torch.int32, device="cuda"))
+            if dist:
+                packed = M.exchange_shard_lists(packed, S)
+            ai, ad, ac = M.unpack_lists(packed, k)
+            oi = torch.zeros((B, k), dtype=torch.int32, device="cuda")
+            od = torch.zeros((B, k), dtype=torch.float32, device="cuda")
+        L.check(lib.raven_merge_topk_device(ai.data_ptr(), ad.data_ptr(), ac.data_ptr(), S, B, k, shard_n,
+                                            oi.data_ptr(), od.data_ptr(), None, stream.cuda_stream))
+        torch.cuda.synchronize()
+        truth.append(oi.cpu().numpy().view(np.uint32))
+    for i in range(max(args.warmup, N_BATCHES)):
+        coll.search(d_q[i % N_BATCHES], params, stream)
+    torch.cuda.synchronize()
+    rec = []
+    for b in range(N_BATCHES):
+        ids, _, _ = coll.search(d_q[b], params, stream)
+        torch.cuda.synchronize()
+        got = ids.cpu().numpy().view(np.uint32)
+        rec += [len(set(got[i]) & set(truth[b][i])) / k for i in range(B)]
+    recall = float(np.mean(rec))
+    clocks = ClockSampler(local)
+    if dist:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        coll.search(d_q[i % N_BATCHES], params, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        tdist.barrier()
+    clk = clocks.stop()
+    ms = M.max_over_ranks(e0.elapsed_time(e1), device=torch.device("cuda", local))
+    value = args.steps * B / (ms / 1e3)
+    # e2e: queries from pinned host memory, ids back to the host, every step
+    hq = torch.from_numpy(qb).pin_memory()
+    h_ids = torch.zeros((B, k), dtype=torch.int32).pin_memory()
+    e2e_steps = max(5, args.steps // 4)
+    if dist:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            dq = hq[i % N_BATCHES].to("cuda", non_blocking=True)
+        ids, _, _ = coll.search(dq, params, stream)
+        with torch.cuda.stream(stream):
+            h_ids.copy_(ids, non_blocking=True)
+        stream.synchronize()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = M.max_over_ranks(f0.elapsed_time(f1), device=torch.device("cuda", local))
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "sq4-int32+f32",
+        "data": "synthetic (seeded Gaussian mixture, per-shard seeds around shared centres)",
+        "config": {
+            "workload": f"{args.workload}: {S} contiguous shards of {shard_n} x "
+                        f"{datasets.WORKLOADS[args.workload]['dim']}, each its own Vamana graph "
+                        f"(R=32 L=200 alpha=1.2 DirectionalPrune nav_m=32) and SQ4 codes; every query on every "
+                        f"shard; SQ4 ef={args.ef} k={k} rr={args.rr}; batch {B} queries per step",
+            "parallelism": f"sharded collection: shard s on rank s % {world}; all-gather of per-shard top-k + "
+                           f"GPU merge (ties by distance, shard, rank)",
+            "shards_per_rank": len(mine), "recall_at_10": round(recall, 4), "queries_scored": len(rec),
+            "index": f"{'GPU-built' if args.build_device is not None else 'host-built or cached'} shard graphs, "
+                     f"rank-0 load/build {build_s:.1f} s",
+            "l2": "not flushed: each rank's shard working set is larger than the 126 MB L2",
+        },
+        "e2e": {"value": e2e_steps * B / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": B * qb.shape[2] * 4,
+                "d2h_bytes_per_step": B * k * 4},
+        "gpu_launches": args.steps * (len(mine) + 1),
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del coll, shards
+    if dist:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.shards:
+        if args.ef is None:
+            args.ef = 50
+        return run_sharded(args)
     if args.ef is None:
         args.ef = OPERATING_EF.get(args.workload, 50)
     import torch

@@ -103,6 +103,25 @@ def make_queries(name: str, nq: int, offset: int = 0) -> np.ndarray:
                           centre_seed=w["seed"] + 500)
 
 
+def make_shard(name: str, shard: int, n_shards: int, shard_n: int | None = None) -> np.ndarray:
+    """Base vectors of one contiguous shard of a workload: shard s holds global
+    ids [s * shard_n, (s + 1) * shard_n) (shard_n = n / n_shards by default),
+    drawn from its own seed around the workload's shared centres, so each rank
+    generates only the shards it holds. The collection is the concatenation of
+    the shards in order; queries come from `make_queries`."""
+    w = WORKLOADS[name]
+    size = w["n"] // n_shards if shard_n is None else shard_n
+    seed = w["seed"] * 1000 + 17 * shard
+    if w["kind"] == "int":
+        return clustered_int(size, w["dim"], w["centres"], w["sigma"], seed, centre_seed=w["seed"] + 500,
+                             zero_frac=w["zero"])
+    return clustered_unit(size, w["dim"], w["centres"], w["sigma"], seed, centre_seed=w["seed"] + 500)
+
+
+def shard_index_path(name: str, shard: int, n_shards: int, shard_n: int) -> str:
+    return _os.path.join(DATA_DIR, f"{name}-shard{shard}of{n_shards}-n{shard_n}.annx")
+
+
 # ---------------------------------------------------------------------------
 # Cached index files (ANNX v1) for the workloads, built with the reference's
 # PyO3 build parameters: R=32, L=200, alpha=1.2, DirectionalPrune, nav_m=32,
