@@ -15,6 +15,8 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import struct
+import zlib
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Tuple
 
@@ -23,6 +25,48 @@ import numpy as np
 from . import _lib as L
 
 SENTINEL = 0xFFFFFFFF
+
+# Base vectors saved beside an ANNX file (`<path>.vec`), so that a saved index
+# can be loaded and searched without the caller supplying the vectors (the
+# ANNX format holds only the graph). Layout, little endian: magic "RVEC" u32,
+# version u32 (1), n u64, dim u32, CRC-32/IEEE of the payload u32, then n*dim
+# f32. SQ parameters, codes and AdaptiveEf samples are recomputed from the
+# vectors on upload (deterministically), so they are not stored.
+_VEC_MAGIC = 0x43455652
+_VEC_HEADER = struct.Struct("<IIQII")
+
+
+def vectors_path(path: str) -> str:
+    return path + ".vec"
+
+
+def save_vectors(path: str, vectors) -> None:
+    v = _f32c(vectors)
+    payload = v.astype("<f4", copy=False).tobytes()
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(_VEC_HEADER.pack(_VEC_MAGIC, 1, v.shape[0], v.shape[1], zlib.crc32(payload) & 0xFFFFFFFF))
+        f.write(payload)
+    os.replace(tmp, path)
+
+
+def load_vectors(path: str) -> np.ndarray:
+    """Read a `.vec` file; IOError on a bad magic, version, size or checksum."""
+    with open(path, "rb") as f:
+        head = f.read(_VEC_HEADER.size)
+        if len(head) != _VEC_HEADER.size:
+            raise IOError(f"{path}: truncated header")
+        magic, version, n, dim, crc = _VEC_HEADER.unpack(head)
+        if magic != _VEC_MAGIC:
+            raise IOError(f"{path}: not a vector file")
+        if version != 1:
+            raise IOError(f"{path}: unsupported version {version}")
+        payload = f.read()
+    if len(payload) != n * dim * 4:
+        raise IOError(f"{path}: expected {n * dim * 4} payload bytes, found {len(payload)}")
+    if zlib.crc32(payload) & 0xFFFFFFFF != crc:
+        raise IOError(f"{path}: checksum mismatch")
+    return np.frombuffer(payload, dtype="<f4").reshape(n, dim).astype(np.float32)
 
 
 def _f32c(x, name="array") -> np.ndarray:
@@ -411,19 +455,23 @@ class Index:
                         device=self.device)
 
     def save(self, path: str) -> None:
+        """The graph as an ANNX file at `path` and, when the index holds its
+        base vectors, `<path>.vec` beside it."""
         if self._graph is None:
             raise RuntimeError("Index not built yet")
         try:
             self._graph.save(path)
         except L.RavenError as e:
             raise IOError(str(e)) from e
+        if self._vectors is not None:
+            save_vectors(vectors_path(path), self._vectors)
 
     @staticmethod
     def load(path: str, dim: int, *, vectors=None, quantization: str = "sq8", rerank_factor: int = 3,
              adaptive_ef: bool = False, device: int = 0) -> "Index":
-        """Index.load (src/python.rs:196-214): sq8, rerank 3. `vectors` supplies
-        the base vectors the file does not hold (without them `searcher()`
-        raises instead of aborting)."""
+        """Index.load (src/python.rs:196-214): sq8, rerank 3. The base vectors
+        come from `vectors`, else from `<path>.vec` when it exists (written by
+        `save`); without either, `searcher()` raises instead of aborting."""
         try:
             g = Graph.load(path)
         except L.RavenError as e:
@@ -431,6 +479,10 @@ class Index:
         ix = Index("L2", dim, quantization=quantization, rerank_factor=rerank_factor, adaptive_ef=adaptive_ef,
                    device=device)
         ix._graph = g
+        if vectors is None and os.path.exists(vectors_path(path)):
+            vectors = load_vectors(vectors_path(path))
+            if vectors.shape != (len(g), dim):
+                raise IOError(f"{vectors_path(path)}: holds {vectors.shape}, expected ({len(g)}, {dim})")
         if vectors is not None:
             v = _f32c(vectors)
             if v.ndim != 2 or v.shape[1] != dim:

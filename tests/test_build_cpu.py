@@ -130,3 +130,25 @@ def test_datasets_are_seeded():
     assert np.allclose(np.linalg.norm(u, axis=1), 1.0, atol=1e-5)
     _, q1 = datasets.make("gmm1m-d128-sparse", n=10, nq=50, query_offset=1)
     assert not np.array_equal(qa, q1)
+
+
+def test_index_save_load_restores_vectors(tmp_path, raven_lib):
+    """Index.save writes the base vectors beside the ANNX file; Index.load
+    restores them, so searcher() works without re-supplying them. A damaged
+    vector file is an IOError."""
+    from raven_b200 import datasets
+    from raven_b200.index import Index, load_vectors, vectors_path
+
+    base, _ = datasets.make("gmm100k-d128", n=1500, nq=1)
+    ix = Index("L2", 128, r=16, l=32, nav_m=8, quantization="sq4")
+    ix.build(base)
+    path = str(tmp_path / "ix.annx")
+    ix.save(path)
+    np.testing.assert_array_equal(load_vectors(vectors_path(path)), base)
+    ix2 = Index.load(path, 128, quantization="sq4")
+    np.testing.assert_array_equal(ix2._vectors, base)
+    raw = bytearray(open(vectors_path(path), "rb").read())
+    raw[100] ^= 0x55
+    open(vectors_path(path), "wb").write(bytes(raw))
+    with pytest.raises(IOError):
+        Index.load(path, 128)

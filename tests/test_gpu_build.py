@@ -75,3 +75,22 @@ def test_gpu_build_search_parity_and_quality(data, oracle):
             np.testing.assert_array_equal(got["ids"], exp["ids"])
             np.testing.assert_array_equal(got["visited"], exp["visited"])
     assert recalls["gpu"] >= recalls["host"] - 0.02, recalls
+
+
+def test_saved_index_serves_without_vectors(tmp_path, raven_lib):
+    """Index.save -> Index.load(path, dim) -> searcher(): the vectors come from
+    the file saved beside the graph; results equal the original searcher's."""
+    from raven_b200 import datasets
+    from raven_b200.index import Index
+
+    base, q = datasets.make("gmm100k-d128", n=3000, nq=100)
+    ix = Index("L2", 128, r=16, l=32, nav_m=8, quantization="sq4", rerank_factor=8)
+    ix.build(base)
+    path = str(tmp_path / "ix.annx")
+    ix.save(path)
+    s1 = ix.searcher()
+    s1.set_ef(50)
+    want = s1.batch_search(q, 10)
+    s2 = Index.load(path, 128, quantization="sq4", rerank_factor=8).searcher()
+    s2.set_ef(50)
+    np.testing.assert_array_equal(s2.batch_search(q, 10), want)
