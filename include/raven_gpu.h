@@ -115,6 +115,7 @@ typedef struct {
   int32_t build_sq4;      /* SQ4Dataset::build (src/quant/sq4.rs:303) on the device */
   int32_t build_sq8;      /* SQ8Dataset::build (src/quant/sq8.rs:395) on the device */
   int32_t build_adaptive; /* AdaptiveEfConfig::build_with_layered_nav samples (src/graph/adaptive_ef.rs:307-327) */
+  int32_t build_f16;      /* F16Dataset::build (src/distance/f16.rs:344-349) for rerank_f16 */
 } raven_upload_options;
 
 /* PyIndex::searcher (src/python.rs:134-181) / GraphSearcher::new + with_sq4/with_sq8
@@ -143,6 +144,8 @@ typedef struct {
   int32_t adaptive;         /* with_adaptive_ef(base.with_params(min_ef, max_ef, gamma)) */
   float gamma;
   uint32_t min_ef, max_ef;
+  int32_t rerank_f16;       /* with_f16 (vamana.rs:1559): rerank with the f16 vectors (rerank_f16,
+                               src/graph/refiner.rs:87-104); needs an index uploaded with build_f16 */
 } raven_search_params;
 
 /* Per-query outputs. ids/dists: nq*k, results in ascending f32 distance,

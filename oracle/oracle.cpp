@@ -103,6 +103,92 @@ float l2_avx512_order(const float* a, const float* b, size_t n) {
   return result + tree16(acc);
 }
 
+// ---------------------------------------------------------------------------
+// f16 rerank arithmetic (src/distance/f16.rs).
+// ---------------------------------------------------------------------------
+
+// F16::from_f32 (f16.rs:26-76) with its exact behaviour: normal results OR the
+// round bit into the truncated mantissa (an odd mantissa is never rounded
+// up), denormal results are truncated, overflow gives Inf, NaN gives 0x7E00.
+uint16_t f16_from_f32(float f) {
+  uint32_t bits;
+  std::memcpy(&bits, &f, 4);
+  const uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+  const int32_t exp = (int32_t)((bits >> 23) & 0xFFu);
+  const uint32_t mant = bits & 0x7FFFFFu;
+  if (exp == 0xFF) return (uint16_t)(sign | (mant ? 0x7E00u : 0x7C00u));
+  const int32_t new_exp = exp - 127 + 15;
+  if (new_exp >= 0x1F) return (uint16_t)(sign | 0x7C00u);
+  if (new_exp <= 0) {
+    if (new_exp < -10) return sign;
+    const uint32_t m = mant | 0x800000u;
+    const int32_t shift = 14 - new_exp;
+    const uint32_t half = 1u << (shift - 1);
+    // the reference's round-up test compares (m & (half-1)) with half: never true
+    const uint32_t up = ((m & (half - 1)) > half || ((m & half) > 0 && (m & (half - 1)) >= half)) ? 1u : 0u;
+    return (uint16_t)(sign | (uint16_t)((m >> shift) + up));
+  }
+  const uint16_t mant_f16 = (uint16_t)(mant >> 13);
+  const uint32_t rem = mant & 0x1FFFu;
+  const uint16_t round = (rem > 0x1000u || (rem == 0x1000u && (mant_f16 & 1u))) ? 1 : 0;
+  uint16_t result = (uint16_t)(sign | ((uint16_t)new_exp << 10) | mant_f16 | round);
+  if ((result & 0x7C00u) == 0x7C00u) result = (uint16_t)(sign | 0x7C00u);
+  return result;
+}
+static float from_bits(uint32_t b) {
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+// F16::to_f32 (f16.rs:86-115), software: exact for normal numbers, a denormal
+// comes out at half its value (the reference's exponent for them is one low).
+float f16_to_f32_soft(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const int32_t exp = (h >> 10) & 0x1F;
+  const uint32_t mant = h & 0x3FFu;
+  if (exp == 0) {
+    if (mant == 0) return from_bits(sign);
+    int32_t e = -1;
+    uint32_t m = mant;
+    while ((m & 0x400u) == 0) {
+      m <<= 1;
+      e -= 1;
+    }
+    m &= 0x3FFu;
+    return from_bits(sign | ((uint32_t)(127 + e - 14) << 23) | (m << 13));
+  }
+  if (exp == 0x1F) return from_bits(sign | 0x7F800000u | (mant << 13));
+  return from_bits(sign | ((uint32_t)(exp - 15 + 127) << 23) | (mant << 13));
+}
+// _mm256_cvtph_ps: IEEE f16 -> f32, exact for every value.
+float f16_to_f32_ieee(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const int32_t exp = (h >> 10) & 0x1F;
+  const uint32_t mant = h & 0x3FFu;
+  if (exp == 0) return from_bits(sign) + (sign ? -1.0f : 1.0f) * std::ldexp((float)mant, -24);
+  if (exp == 0x1F) return from_bits(sign | 0x7F800000u | (mant << 13));
+  return from_bits(sign | ((uint32_t)(exp - 15 + 127) << 23) | (mant << 13));
+}
+// l2_f16_mixed_avx512 (f16.rs:213-262): 16 lane accumulators over chunks with
+// hardware conversion, fma(d, d, acc); the tail element by element with the
+// software conversion and a separate multiply and add; result = tail + tree.
+float l2_f16_mixed_avx512_order(const float* q, const uint16_t* db, size_t n) {
+  const size_t chunks = n / 16, rem = n % 16;
+  float acc[16];
+  for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+  for (size_t c = 0; c < chunks; ++c)
+    for (int j = 0; j < 16; ++j) {
+      const float d = q[c * 16 + j] - f16_to_f32_ieee(db[c * 16 + j]);
+      acc[j] = std::fma(d, d, acc[j]);
+    }
+  float result = 0.0f;
+  for (size_t i = 0; i < rem; ++i) {
+    const float d = q[chunks * 16 + i] - f16_to_f32_soft(db[chunks * 16 + i]);
+    result += d * d;  // built with -ffp-contract=off: a multiply then an add
+  }
+  return result + tree16(acc);
+}
+
 // src/distance/avx2.rs:26-54,86-98 — 8 lanes, horizontal_sum_ps
 // ((hi+lo) 4 lanes, then movehdup/movehl adds), then a sequential fma tail.
 float l2_avx2_order(const float* a, const float* b, size_t n) {
@@ -308,6 +394,7 @@ struct Index {
   SQParams sq4, sq8;
   std::vector<uint8_t> sq4_codes, sq8_codes;
   size_t sq4_bytes = 0;
+  std::vector<uint16_t> f16;  // F16Dataset::build (src/distance/f16.rs:344-349), for with_f16
   // AdaptiveEf samples (sorted) — src/graph/adaptive_ef.rs:307-327
   std::vector<float> adaptive_samples;
 };
@@ -525,14 +612,17 @@ inline int32_t total_key(float f) {
 // sort_unstable_by(total_cmp), whose order among equal distances is
 // unspecified; this restatement (and the CUDA engine) breaks ties by the
 // candidate's position in the SQ search result (stable by pool order).
+// With `f16` set: rerank_f16 / F16Refiner::rerank (src/graph/refiner.rs:87-104,
+// 132-end), the same rule with l2_f16_mixed_simd on the f16 vectors.
 std::vector<std::pair<uint32_t, float>> rerank_f32(const Index& ix, const float* q,
                                                    const std::vector<std::pair<uint32_t, float>>& cands,
-                                                   size_t k, size_t rr) {
+                                                   size_t k, size_t rr, bool f16 = false) {
   size_t rerank_n = std::min(std::max(k * rr, k), cands.size());
   std::vector<std::pair<uint32_t, float>> res(rerank_n);
   for (size_t i = 0; i < rerank_n; ++i) {
     uint32_t id = cands[i].first;
-    res[i] = {id, l2_avx512_order(q, ix.vectors.data() + (size_t)id * ix.dim, ix.dim)};
+    res[i] = {id, f16 ? l2_f16_mixed_avx512_order(q, ix.f16.data() + (size_t)id * ix.dim, ix.dim)
+                      : l2_avx512_order(q, ix.vectors.data() + (size_t)id * ix.dim, ix.dim)};
   }
   std::stable_sort(res.begin(), res.end(), [](const std::pair<uint32_t, float>& a,
                                               const std::pair<uint32_t, float>& b) {
@@ -550,6 +640,7 @@ struct OracleParams {
   uint32_t adaptive;
   float gamma;
   uint32_t min_ef, max_ef;
+  uint32_t rerank_f16;  // 1: GraphSearcher::with_f16 (src/graph/vamana.rs:1559, 1824-1828)
 };
 
 struct QueryOut {
@@ -613,7 +704,7 @@ int search_one(const Index& ix, const float* q, const OracleParams& p, Worker& w
   out->expansions = st.expansions;
   if (want_history) out->history = w.visited.history;
   size_t rr = std::max<uint32_t>(p.rerank_factor, 1);  // with_rerank_factor clamps >= 1 (:1547-1550)
-  out->results = rerank_f32(ix, q, cands, p.k, rr);
+  out->results = rerank_f32(ix, q, cands, p.k, rr, p.rerank_f16 != 0);
   return 0;
 }
 
@@ -772,6 +863,17 @@ int oracle_index_set_vectors(void* h, const float* vectors, uint64_t n, uint32_t
   }
   return 0;
 }
+// F16Dataset::build for with_f16 reranks.
+int oracle_index_build_f16(void* h) {
+  Index* ix = (Index*)h;
+  if (ix->vectors.empty()) { g_err = "set_vectors first"; return -7; }
+  ix->f16.resize(ix->vectors.size());
+  for (size_t i = 0; i < ix->vectors.size(); ++i) ix->f16[i] = f16_from_f32(ix->vectors[i]);
+  return 0;
+}
+uint16_t oracle_f16_from_f32(float f) { return f16_from_f32(f); }
+float oracle_f16_to_f32(uint16_t h) { return f16_to_f32_soft(h); }
+float oracle_l2_f16_mixed(const float* q, const uint16_t* db, size_t n) { return l2_f16_mixed_avx512_order(q, db, n); }
 size_t oracle_index_adaptive_samples(void* h, const float** out) {
   Index* ix = (Index*)h;
   *out = ix->adaptive_samples.data();
@@ -812,6 +914,7 @@ int oracle_search_batch(void* h, const float* queries, uint64_t nq, const Oracle
   if (ix->vectors.empty()) { g_err = "vectors not set"; return -8; }
   if (p->quant == 0 && ix->sq4_codes.empty()) { g_err = "sq4 not built"; return -8; }
   if (p->quant == 1 && ix->sq8_codes.empty()) { g_err = "sq8 not built"; return -8; }
+  if (p->rerank_f16 && ix->f16.empty()) { g_err = "f16 vectors not built"; return -8; }
   if (threads <= 0) threads = (int)std::thread::hardware_concurrency();
   if (threads <= 0) threads = 1;
   std::atomic<uint64_t> next(0);

@@ -21,13 +21,18 @@ u8p = C.POINTER(C.c_uint8)
 
 class OracleParams(C.Structure):
     _fields_ = [("ef", C.c_uint32), ("k", C.c_uint32), ("rerank_factor", C.c_uint32), ("quant", C.c_uint32),
-                ("adaptive", C.c_uint32), ("gamma", C.c_float), ("min_ef", C.c_uint32), ("max_ef", C.c_uint32)]
+                ("adaptive", C.c_uint32), ("gamma", C.c_float), ("min_ef", C.c_uint32), ("max_ef", C.c_uint32),
+                ("rerank_f16", C.c_uint32)]
 
 
 _SIG = {
     "oracle_last_error": (C.c_char_p, []),
     "oracle_crc32": (C.c_uint32, [C.c_void_p, C.c_size_t]),
     "oracle_l2_avx512": (C.c_float, [f32p, f32p, C.c_size_t]),
+    "oracle_f16_from_f32": (C.c_uint16, [C.c_float]),
+    "oracle_f16_to_f32": (C.c_float, [C.c_uint16]),
+    "oracle_l2_f16_mixed": (C.c_float, [f32p, C.POINTER(C.c_uint16), C.c_size_t]),
+    "oracle_index_build_f16": (C.c_int, [C.c_void_p]),
     "oracle_l2_avx2": (C.c_float, [f32p, f32p, C.c_size_t]),
     "oracle_l2_sq4_raw": (C.c_float, [u8p, u8p, C.c_size_t]),
     "oracle_l2_sq8_raw": (C.c_float, [u8p, u8p, C.c_size_t]),
@@ -101,6 +106,20 @@ def l2_avx512(a, b) -> float:
     a = np.ascontiguousarray(a, np.float32)
     b = np.ascontiguousarray(b, np.float32)
     return float(lib().oracle_l2_avx512(_p(a, C.c_float), _p(b, C.c_float), a.size))
+
+
+def f16_from_f32(x: float) -> int:
+    return int(lib().oracle_f16_from_f32(float(x)))
+
+
+def f16_to_f32(h: int) -> float:
+    return float(lib().oracle_f16_to_f32(int(h)))
+
+
+def l2_f16_mixed(q, db_f16) -> float:
+    q = np.ascontiguousarray(q, np.float32)
+    d = np.ascontiguousarray(db_f16, np.uint16)
+    return float(lib().oracle_l2_f16_mixed(_p(q, C.c_float), d.ctypes.data_as(C.POINTER(C.c_uint16)), q.size))
 
 
 def l2_avx2(a, b) -> float:
@@ -238,11 +257,13 @@ class OracleIndex:
         n = lib().oracle_index_nav_candidates(self.h, C.byref(p))
         return np.ctypeslib.as_array(p, shape=(n,)).copy() if n else np.zeros(0, np.uint32)
 
-    def set_vectors(self, vectors, sq4=True, sq8=False, adaptive=False):
+    def set_vectors(self, vectors, sq4=True, sq8=False, adaptive=False, f16=False):
         v = np.ascontiguousarray(vectors, np.float32)
         self._vectors = v
         rc = lib().oracle_index_set_vectors(self.h, _p(v, C.c_float), v.shape[0], v.shape[1], int(sq4), int(sq8),
                                             int(adaptive))
+        if rc == 0 and f16:
+            rc = lib().oracle_index_build_f16(self.h)
         if rc != 0:
             raise RuntimeError(lib().oracle_last_error().decode())
 
@@ -268,11 +289,11 @@ class OracleIndex:
         return int(e.value), float(d.value), int(n.value)
 
     def search(self, queries, k=10, ef=50, rerank_factor=5, quant=0, adaptive=False, gamma=2.0, min_ef=30,
-               max_ef=100, threads=0, history_cap=0) -> dict:
+               max_ef=100, threads=0, history_cap=0, rerank_f16=False) -> dict:
         q = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
         nq = q.shape[0]
         p = OracleParams(ef=ef, k=k, rerank_factor=rerank_factor, quant=quant, adaptive=int(adaptive), gamma=gamma,
-                         min_ef=min_ef, max_ef=max_ef)
+                         min_ef=min_ef, max_ef=max_ef, rerank_f16=int(rerank_f16))
         r = {"ids": np.zeros((nq, k), np.uint32), "dists": np.zeros((nq, k), np.float32),
              "counts": np.zeros(nq, np.uint32), "visited": np.zeros(nq, np.uint32),
              "ef_used": np.zeros(nq, np.uint32), "n_nav": np.zeros(nq, np.uint32),

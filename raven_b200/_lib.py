@@ -68,6 +68,7 @@ class UploadOptions(C.Structure):
         ("build_sq4", C.c_int32),
         ("build_sq8", C.c_int32),
         ("build_adaptive", C.c_int32),
+        ("build_f16", C.c_int32),
     ]
 
 
@@ -82,6 +83,7 @@ class SearchParams(C.Structure):
         ("gamma", C.c_float),
         ("min_ef", C.c_uint32),
         ("max_ef", C.c_uint32),
+        ("rerank_f16", C.c_int32),
     ]
 
 

@@ -40,6 +40,7 @@ struct raven_index {
   uint64_t n = 0;
   uint32_t dim = 0, dim_pad = 0, r_max = 0, r_pad = 0, entry = 0;
   float* d_vec = nullptr;
+  uint16_t* d_vec16 = nullptr;  // f16 copy for with_f16 reranks (F16Dataset), lane-major like d_vec
   uint32_t* d_adj = nullptr;
   bool has_q[2] = {false, false};
   uint32_t q_stride[2] = {0, 0};
@@ -363,6 +364,37 @@ __global__ void tc_base_split_kernel(const float* __restrict__ vec, uint64_t tot
   }
 }
 
+// F16::from_f32 (src/distance/f16.rs:26-76) with the reference's exact
+// behaviour: normal results OR the round bit into the truncated mantissa (an
+// odd mantissa is never rounded up), denormal results are truncated, overflow
+// gives Inf, NaN gives 0x7E00.
+__device__ inline uint16_t f16_from_f32_ref(float f) {
+  const uint32_t bits = __float_as_uint(f);
+  const uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+  const int32_t exp = (int32_t)((bits >> 23) & 0xFFu);
+  const uint32_t mant = bits & 0x7FFFFFu;
+  if (exp == 0xFF) return (uint16_t)(sign | (mant ? 0x7E00u : 0x7C00u));
+  const int32_t new_exp = exp - 127 + 15;
+  if (new_exp >= 0x1F) return (uint16_t)(sign | 0x7C00u);
+  if (new_exp <= 0) {
+    if (new_exp < -10) return sign;
+    const uint32_t m = mant | 0x800000u;
+    return (uint16_t)(sign | (uint16_t)(m >> (14 - new_exp)));
+  }
+  const uint16_t mant_f16 = (uint16_t)(mant >> 13);
+  const uint32_t rem = mant & 0x1FFFu;
+  const uint16_t round = (rem > 0x1000u || (rem == 0x1000u && (mant_f16 & 1u))) ? 1 : 0;
+  uint16_t result = (uint16_t)(sign | ((uint16_t)new_exp << 10) | mant_f16 | round);
+  if ((result & 0x7C00u) == 0x7C00u) result = (uint16_t)(sign | 0x7C00u);
+  return result;
+}
+// The element-wise conversion commutes with the lane-major permutation, so
+// the f16 rows are converted straight from the device's f32 rows.
+__global__ void f16_convert_kernel(const float* __restrict__ in, uint64_t total, uint16_t* __restrict__ out) {
+  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
+    out[t] = f16_from_f32_ref(in[t]);
+}
+
 // Shard merge: ids are shard-local; global id = shard * shard_size + local.
 __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ ds,
                                    const uint32_t* __restrict__ counts, uint32_t n_shards, uint64_t nq, uint32_t k,
@@ -475,6 +507,8 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
     return fail(RAVEN_ESTATE, p->quant == 0 ? "search_sq4 requires with_sq4() first (index uploaded without SQ4)"
                                             : "search_sq8 requires with_sq8() first (index uploaded without SQ8)");
   if (p->k == 0) return fail(RAVEN_EINVAL, "k must be >= 1");
+  if (p->rerank_f16 && !ix->d_vec16)
+    return fail(RAVEN_ESTATE, "with_f16 requires an index uploaded with build_f16");
   pl->quant = p->quant;
   pl->cpl = (int)(ix->q_stride[p->quant] / 16);
   uint32_t ef_cap;
@@ -565,6 +599,8 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.vec_rem = ix->dim % 16;
   a.adj = ix->d_adj;
   a.r_pad = ix->r_pad;
+  a.vec16 = ix->d_vec16;
+  a.rerank_f16 = (!nav_only && p->rerank_f16) ? 1 : 0;
   a.pool_cap = pl.pool_cap;
   a.codes = ix->d_codes[pl.quant];
   a.code_stride = ix->q_stride[pl.quant];
@@ -634,6 +670,7 @@ void free_index(raven_index* ix) {
   if (!ix) return;
   cudaSetDevice(ix->device);
   cudaFree(ix->d_vec);
+  cudaFree(ix->d_vec16);
   cudaFree(ix->d_adj);
   for (int q = 0; q < 2; ++q) {
     cudaFree(ix->d_codes[q]);
@@ -759,7 +796,7 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
   if (dim != g.dim) return fail(RAVEN_EINVAL, "dim mismatch: expected " + std::to_string(g.dim) + ", got " + std::to_string(dim));
   if (n == 0) return fail(RAVEN_EINVAL, "empty index");
   if (n >= 0x7FFFFFFFull) return fail(RAVEN_ELIMIT, "node ids must fit in 31 bits");
-  raven_upload_options o{0, 1, 0, 0};
+  raven_upload_options o{0, 1, 0, 0, 0};
   if (opt) o = *opt;
   if (g.r_max > kMaxR) return fail(RAVEN_ELIMIT, "graph degree above the engine limit of 128");
   if (o.build_sq4 && dim > kMaxDimSq4) return fail(RAVEN_ELIMIT, "dim above the SQ4 engine limit of 256");
@@ -890,6 +927,11 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
                                                                   ix->d_nav_vec);
       if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "nav gather failed"));
     }
+  }
+  if (o.build_f16) {
+    if (cudaMalloc((void**)&ix->d_vec16, n * dim * 2) != cudaSuccess) return bail2(fail(RAVEN_ENOMEM, "f16 vectors"));
+    f16_convert_kernel<<<ix->num_sms * 4, 256, 0, ix->stream>>>(ix->d_vec, n * dim, ix->d_vec16);
+    if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "f16 conversion failed"));
   }
   if (cudaStreamSynchronize(ix->stream) != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "upload failed"));
   // AdaptiveEf samples: nav.initialize distances of base vectors 0..min(n,2000)
@@ -1341,6 +1383,8 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   a.vec_rem = ix->dim % 16;
   a.adj = ix->d_adj;
   a.r_pad = ix->r_pad;
+  a.vec16 = ix->d_vec16;
+  a.rerank_f16 = p->rerank_f16 ? 1 : 0;
   a.pool_cap = pl.pool_cap;
   a.codes = ix->d_codes[pl.quant];
   a.code_stride = ix->q_stride[pl.quant];
@@ -1432,7 +1476,6 @@ __global__ void __launch_bounds__(kPruneThreads) build_prune_kernel(
   uint32_t* kept_id = kept_bits + bit_words;                   // r_max (+ pad)
   float* rows = (float*)(kept_id + ((r_max + 3u) & ~3u));      // r_max kept rows, then 16 candidate rows
   float* crow = rows + (size_t)r_max * stride;
-  __shared__ int viol;
   __shared__ uint32_t nk, ncand;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, h = lane >> 4, j = lane & 15;
   const uint32_t b = blockIdx.x;
@@ -1606,7 +1649,7 @@ struct GpuBuild : raven::BuildAccelerator {
       while (d < r && main_block[v * r + d] != raven::kSentinel) ++d;
       gr.g.degrees[v] = d;
     }
-    raven_upload_options o{device, 1, 0, 0};
+    raven_upload_options o{device, 1, 0, 0, 0};
     int rc = raven_index_upload(&gr, h_vec, n_, dim, &o, &ix);
     if (rc) {
       if (err) *err = raven_last_error();

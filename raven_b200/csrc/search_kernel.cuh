@@ -23,6 +23,7 @@
 // follows unpermuted. Lane j of a half-warp then reads its whole fma chain
 // (elements j, 16+j, 32+j, ...) contiguously, in the reference's order.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -47,6 +48,8 @@ struct SearchArgs {
   const uint32_t* __restrict__ adj;
   uint32_t r_pad;  // row stride in ids (multiple of 32)
   uint32_t pool_cap;  // beam pool capacity per warp (multiple of 32, >= every query's ef)
+  const uint16_t* vec16;  // n x dim f16, lane-major (with_f16), or null
+  int rerank_f16;         // 1: rerank with the f16 vectors
   const uint8_t* __restrict__ codes;
   uint32_t code_stride;  // bytes per code row (power of two, >= 16)
   const float* __restrict__ q_inv;
@@ -247,6 +250,95 @@ __device__ inline float hw_dist(const float* __restrict__ qf, const float* __res
     tail = tree16(__fmaf_rn(d, d, 0.0f));
   }
   return __fadd_rn(tail, tree16(acc));
+}
+
+// ---------------------------------------------------------------------------
+// f16 rerank (GraphSearcher::with_f16, src/graph/vamana.rs:1559, 1824-1828).
+// ---------------------------------------------------------------------------
+// F16::to_f32 (src/distance/f16.rs:86-115) as the reference computes it in
+// software: exact for normal numbers; a denormal comes out at half its value.
+__device__ inline float f16_to_f32_soft(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const int32_t exp = (h >> 10) & 0x1F;
+  const uint32_t mant = h & 0x3FFu;
+  if (exp == 0) {
+    if (mant == 0) return __uint_as_float(sign);
+    int32_t e = -1;
+    uint32_t m = mant;
+    while ((m & 0x400u) == 0) {
+      m <<= 1;
+      e -= 1;
+    }
+    return __uint_as_float(sign | ((uint32_t)(127 + e - 14) << 23) | ((m & 0x3FFu) << 13));
+  }
+  if (exp == 0x1F) return __uint_as_float(sign | 0x7F800000u | (mant << 13));
+  return __uint_as_float(sign | ((uint32_t)(exp - 15 + 127) << 23) | (mant << 13));
+}
+
+// l2_f16_mixed_avx512 (src/distance/f16.rs:213-262) by a half-warp, against a
+// lane-major f16 row: lane j's fma chain over c (hardware f16 -> f32, exact),
+// the tree; the dim%16 tail element by element with the software conversion
+// and a separate multiply and add (every lane computes it; same value);
+// result = tail + tree.
+__device__ inline float hw_dist_f16(const float* __restrict__ qf, const uint16_t* __restrict__ row, uint32_t C,
+                                   uint32_t rem, int j) {
+  float acc = 0.0f;
+  const float* q = qf + j * C;
+  const uint16_t* r = row + j * C;
+  for (uint32_t c = 0; c < C; ++c) {
+    const float d = __fsub_rn(q[c], __half2float(__ushort_as_half(r[c])));
+    acc = __fmaf_rn(d, d, acc);
+  }
+  float tail = 0.0f;
+  for (uint32_t i = 0; i < rem; ++i) {
+    const float d = __fsub_rn(qf[16 * C + i], f16_to_f32_soft(row[16 * C + i]));
+    tail = __fadd_rn(tail, __fmul_rn(d, d));
+  }
+  return __fadd_rn(tail, tree16(acc));
+}
+
+// Stage `nrows` f16 rows (dim halves each, row r from row_ptr(r)) at stage +
+// r*dim; 16-byte copies when rows are multiples of 8 halves, 4-byte copies for
+// even dims, plain loads otherwise. All lanes issue, then wait.
+template <class RowPtr>
+__device__ inline void stage_rows_f16(uint16_t* stage, int nrows, uint32_t dim, RowPtr row_ptr, int lane) {
+  if ((dim & 7u) == 0) {
+    const uint32_t per = dim >> 3;
+    for (uint32_t t = lane; t < (uint32_t)nrows * per; t += 32) {
+      const uint32_t r = t / per, o = t - r * per;
+      cp_async16(stage + r * dim + o * 8, row_ptr(r) + o * 8);
+    }
+  } else if ((dim & 1u) == 0) {
+    const uint32_t per = dim >> 1;
+    for (uint32_t t = lane; t < (uint32_t)nrows * per; t += 32) {
+      const uint32_t r = t / per, o = t - r * per;
+      cp_async4(stage + r * dim + o * 2, row_ptr(r) + o * 2);
+    }
+  } else {
+    for (uint32_t t = lane; t < (uint32_t)nrows * dim; t += 32) {
+      const uint32_t r = t / dim, o = t - r * dim;
+      stage[r * dim + o] = row_ptr(r)[o];
+    }
+  }
+  cp_async_wait_all();
+  __syncwarp();
+}
+
+template <class RowPtr>
+__device__ inline void rows_dist_f16(const float* qf, uint16_t* stage, uint32_t stage_rows_max, const uint32_t* ids,
+                                     int n, uint32_t dim, uint32_t C, uint32_t rem, RowPtr row_ptr, float* out,
+                                     int lane) {
+  const int h = lane >> 4, j = lane & 15;
+  for (int b0 = 0; b0 < n; b0 += (int)stage_rows_max) {
+    const int nb = min((int)stage_rows_max, n - b0);
+    stage_rows_f16(stage, nb, dim, [&](uint32_t r) { return row_ptr(ids[b0 + r]); }, lane);
+    for (int r0 = 0; r0 < nb; r0 += 2) {
+      const int r = min(r0 + h, nb - 1);
+      const float d = hw_dist_f16(qf, stage + (size_t)r * dim, C, rem, j);
+      if (j == 0 && r0 + h < nb) out[b0 + r0 + h] = d;
+    }
+    __syncwarp();
+  }
 }
 
 // Distances of `n` rows (handles/ids in `ids` smem, resolved by row_ptr) into
@@ -943,7 +1035,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       const int cn = min(32, rn - c0);
       if (lane < cn) s.cand_id[lane] = s.pool_id[c0 + lane] & ~kChecked;
       __syncwarp();
-      rows_dist(s.qf, stage, stage_rows_max, s.cand_id, cn, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd, lane);
+      if (a.rerank_f16)
+        rows_dist_f16(s.qf, (uint16_t*)s.ht, min(32u, (H * 4u) / (a.dim * 2u)), s.cand_id, cn, a.dim, a.vec_c,
+                      a.vec_rem, [&](uint32_t id) { return a.vec16 + (size_t)id * a.dim; }, s.nd, lane);
+      else
+        rows_dist(s.qf, stage, stage_rows_max, s.cand_id, cn, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd, lane);
       if (lane < cn) rdist[c0 + lane] = s.nd[lane];
       __syncwarp();
     }

@@ -162,19 +162,20 @@ class DeviceIndex:
     """Graph + vectors + quantised codes resident in one GPU's HBM."""
 
     def __init__(self, graph: Graph, vectors, device: int = 0, sq4: bool = True, sq8: bool = False,
-                 adaptive: bool = False):
+                 adaptive: bool = False, f16: bool = False):
         lib = L.load()
         v = _f32c(vectors)
         if v.ndim != 2:
             raise ValueError("vectors must be a 2-D float32 array")
-        opt = L.UploadOptions(device=device, build_sq4=int(sq4), build_sq8=int(sq8), build_adaptive=int(adaptive))
+        opt = L.UploadOptions(device=device, build_sq4=int(sq4), build_sq8=int(sq8), build_adaptive=int(adaptive),
+                              build_f16=int(f16))
         h = C.c_void_p()
         L.check(lib.raven_index_upload(graph._h, L.ptr(v, C.c_float), v.shape[0], v.shape[1], C.byref(opt),
                                        C.byref(h)))
         self._h = h
         self.n, self.dim = v.shape
         self.device = device
-        self.has_sq4, self.has_sq8, self.has_adaptive = sq4, sq8, adaptive
+        self.has_sq4, self.has_sq8, self.has_adaptive, self.has_f16 = sq4, sq8, adaptive, f16
 
     def adaptive_samples(self) -> np.ndarray:
         n = C.c_uint32()
@@ -266,6 +267,7 @@ class GraphSearcher:
         self._quant: Optional[int] = None  # None: with_sq4/with_sq8 not called
         self._want = {"sq4": False, "sq8": False}
         self._adaptive: Optional[AdaptiveEfConfig] = None
+        self._f16 = False  # with_f16: rerank with f16 vectors
         self._device = device
         self._dev: Optional[DeviceIndex] = None
         self._last_visited = 0
@@ -289,6 +291,14 @@ class GraphSearcher:
         self._dev = None
         return self
 
+    def with_f16(self, f16=None) -> "GraphSearcher":
+        """GraphSearcher::with_f16 (src/graph/vamana.rs:1559): rerank with the
+        vectors converted to f16 (F16Dataset::build), as rerank_f16 does."""
+        self._f16 = True
+        if self._dev is not None and not self._dev.has_f16:
+            self._dev = None
+        return self
+
     def with_adaptive_ef(self, config: AdaptiveEfConfig) -> "GraphSearcher":
         self._adaptive = config
         if self._dev is not None and not self._dev.has_adaptive:
@@ -298,13 +308,13 @@ class GraphSearcher:
     def _device_index(self) -> DeviceIndex:
         if self._dev is None:
             self._dev = DeviceIndex(self._graph, self._vectors, device=self._device, sq4=self._want["sq4"],
-                                    sq8=self._want["sq8"], adaptive=self._adaptive is not None)
+                                    sq8=self._want["sq8"], adaptive=self._adaptive is not None, f16=self._f16)
         return self._dev
 
     def _params(self, k: int, quant: int) -> L.SearchParams:
         p = L.SearchParams(ef=self.ef_search, k=k, rerank_factor=self.rerank_factor,
                            prefetch_offset=self.prefetch_offset, quant=quant, adaptive=0, gamma=0.0, min_ef=0,
-                           max_ef=0)
+                           max_ef=0, rerank_f16=int(self._f16))
         if self._adaptive is not None:
             p.adaptive = 1
             p.gamma = self._adaptive.gamma

@@ -416,3 +416,24 @@ def test_odd_dim_parity(oracle, raven_lib, dim):
         got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, quant=quant), history_cap=4096)
         exp = oi.search(q, k=10, ef=50, rerank_factor=8, quant=quant, history_cap=4096)
         _compare(got, exp)
+
+
+@pytest.mark.parametrize("dim", [128, 70, 75])
+def test_f16_rerank_parity(oracle, raven_lib, dim):
+    """GraphSearcher::with_f16: rerank on the f16 vectors (F16Dataset) with
+    l2_f16_mixed's order, on float data so the conversion rounds; 16-byte,
+    4-byte and plain-load staging of the f16 rows."""
+    from raven_b200 import datasets
+    from raven_b200.index import DeviceIndex, Graph
+
+    base = datasets.clustered_unit(3000, dim, 30, 0.3, seed=dim, centre_seed=dim + 1) * 3.0
+    q = datasets.clustered_unit(200, dim, 30, 0.3, seed=dim + 2, centre_seed=dim + 1) * 3.0
+    g = Graph.build(base, r=32, l=64, alpha=1.2, nav_m=8, directional=True, seed=3)
+    dev = DeviceIndex(g, base, sq4=True, f16=True)
+    oi = _oracle_for(oracle, g, base, sq8=False, adaptive=False)
+    oi.set_vectors(base, sq4=True, f16=True)
+    got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, rerank_f16=1), history_cap=4096)
+    exp = oi.search(q, k=10, ef=50, rerank_factor=8, history_cap=4096, rerank_f16=True)
+    _compare(got, exp)
+    f32 = oi.search(q, k=10, ef=50, rerank_factor=8)
+    assert not np.array_equal(exp["dists"], f32["dists"])  # the f16 path really differs from the f32 one

@@ -332,3 +332,42 @@ def test_degree_is_first_sentinel(oracle):
     oi = oracle.OracleIndex(data=b)
     assert oi.neighbors(0).tolist() == [1, 2]
     assert oi.neighbors(2).tolist() == [0, 1, 3]
+
+
+# F16::from_f32 / to_f32 / l2_f16_mixed known answers (src/distance/f16.rs:380-470 tests)
+def test_f16_conversion_kat(oracle):
+    assert oracle.f16_from_f32(0.0) == 0
+    assert oracle.f16_from_f32(-0.0) == 0x8000
+    assert oracle.f16_from_f32(float("inf")) == 0x7C00
+    assert oracle.f16_from_f32(float("-inf")) == 0xFC00
+    assert oracle.f16_from_f32(70000.0) & 0x7C00 == 0x7C00  # above 65504: Inf
+    for v in (1.0, 2.0, 3.0, 0.5, -1.5, 100.0, 0.001):
+        r = oracle.f16_to_f32(oracle.f16_from_f32(v))
+        assert abs(r - v) / max(v, 1e-6) < 0.01
+    vals = [i / 100.0 for i in range(100)]
+    assert max(abs(oracle.f16_to_f32(oracle.f16_from_f32(v)) - v) for v in vals) < 0.001
+    # integers up to 2048 are exact
+    for i in range(0, 2049, 7):
+        assert oracle.f16_to_f32(oracle.f16_from_f32(float(i))) == float(i)
+
+
+def test_f16_rounding_follows_reference(oracle):
+    # the reference ORs the round bit into the truncated mantissa: an even
+    # mantissa rounds up past half, an odd one never does
+    one_plus = np.float32(1.0) + np.float32(2.0 ** -10)  # mantissa ...01 (odd), exact in f16
+    assert oracle.f16_from_f32(float(one_plus)) == 0x3C01
+    above_even = np.float32(1.0) + np.float32(2.0 ** -11) * 1.5  # even mantissa, remainder above half
+    assert oracle.f16_from_f32(float(above_even)) == 0x3C01
+    above_odd = np.float32(1.0) + np.float32(2.0 ** -10) + np.float32(2.0 ** -11) * 1.5  # odd, above half
+    assert oracle.f16_from_f32(float(above_odd)) == 0x3C01  # IEEE would give 0x3C02
+
+
+def test_l2_f16_mixed_kat(oracle):
+    q = np.array([1.0, 2.0, 3.0], np.float32)
+    db = np.array([oracle.f16_from_f32(x) for x in (4.0, 5.0, 6.0)], np.uint16)
+    assert abs(oracle.l2_f16_mixed(q, db) - 27.0) < 0.5
+    q = (np.arange(128) / 128.0).astype(np.float32)
+    dbf = (np.arange(128) / 128.0 * 0.9).astype(np.float32)
+    db = np.array([oracle.f16_from_f32(float(x)) for x in dbf], np.uint16)
+    exact = float(np.sum((q.astype(np.float64) - dbf) ** 2))
+    assert abs(oracle.l2_f16_mixed(q, db) - exact) / exact < 0.01
