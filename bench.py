@@ -266,7 +266,10 @@ def run_sharded(args):
         if os.path.exists(path):
             g = Graph.load(path)
         else:
+            # torchrun sets OMP_NUM_THREADS=1: give each rank's host part of the
+            # build its share of the cores explicitly
             g = Graph.build(base, r=32, l=200, alpha=1.2, nav_m=32, directional=True, seed=42 + sh,
+                            threads=max(1, (os.cpu_count() or 1) // world),
                             device=local if args.build_device is not None else None)
             os.makedirs(os.path.dirname(path), exist_ok=True)
             g.save(path + ".tmp")
