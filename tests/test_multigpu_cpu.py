@@ -136,3 +136,15 @@ def test_merge_rule_ties(oracle):
     c = np.array([[2], [2]], np.uint32)
     i, dd, cc = oracle.merge_shard_lists(ids, d, c, 100, 3)
     assert i.tolist() == [[5, 107, 108]] and dd.tolist() == [[1.0, 1.0, 1.5]] and cc.tolist() == [3]
+
+
+def test_make_shard_deterministic_and_distinct():
+    from raven_b200 import datasets
+
+    a = datasets.make_shard("gmm40m-d128", 3, 8, shard_n=500)
+    b = datasets.make_shard("gmm40m-d128", 3, 8, shard_n=500)
+    c = datasets.make_shard("gmm40m-d128", 4, 8, shard_n=500)
+    assert a.shape == (500, 128) and a.dtype == np.float32
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    assert np.all(a == np.rint(a)) and a.min() >= 0 and a.max() <= 255
+    assert datasets.shard_index_path("gmm40m-d128", 3, 8, 500).endswith("gmm40m-d128-shard3of8-n500.annx")
