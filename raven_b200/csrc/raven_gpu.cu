@@ -11,6 +11,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
@@ -60,6 +61,15 @@ struct raven_index {
 };
 
 namespace {
+
+// NVTX range around a host-side phase (upload, search, exact kNN, merge,
+// build batches): shows on a profiler's timeline, no cost without one.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 thread_local std::string g_err;
 
@@ -704,6 +714,7 @@ void raven_limits(raven_limits_t* out) {
 
 int raven_graph_build(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg,
                       raven_graph** out) {
+  NvtxRange nvtx_range("raven.graph_build");
   if (!out || (!vectors && n) || !cfg) return fail(RAVEN_EINVAL, "null argument");
   raven::BuildConfig c;
   c.alpha = cfg->alpha;
@@ -790,6 +801,7 @@ int raven_graph_neighbors(const raven_graph* g, uint32_t node, uint32_t* out, ui
 
 int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, uint32_t dim,
                        const raven_upload_options* opt, raven_index** out) {
+  NvtxRange nvtx_range("raven.index_upload");
   if (!gr || !out || (!vectors && n)) return fail(RAVEN_EINVAL, "null argument");
   const raven::HostGraph& g = gr->g;
   if (n != g.n) return fail(RAVEN_EINVAL, "vector count does not match the graph");
@@ -997,6 +1009,7 @@ int raven_index_codes(const raven_index* ix, int32_t quant, uint8_t* out, uint64
 
 int raven_search_batch_device(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
                               const raven_search_outputs* d_out, void* stream) {
+  NvtxRange nvtx_range("raven.search_batch_device");
   if (!ix) return fail(RAVEN_EINVAL, "null index");
   if (nq && !d_q) return fail(RAVEN_EINVAL, "null queries");
   cudaStream_t st = (cudaStream_t)stream;  // NULL: the CUDA default stream
@@ -1005,6 +1018,7 @@ int raven_search_batch_device(raven_index* ix, const float* d_q, uint64_t nq, co
 
 int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven_search_params* p,
                        const raven_search_outputs* out, void* stream) {
+  NvtxRange nvtx_range("raven.search_batch");
   if (!ix) return fail(RAVEN_EINVAL, "null index");
   if (!out || !out->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
   if (!p) return fail(RAVEN_EINVAL, "null search params");
@@ -1141,6 +1155,7 @@ extern "C" {
 
 int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint32_t k, uint32_t* d_ids,
                            float* d_dists, void* stream) {
+  NvtxRange nvtx_range("raven.knn_exact");
   if (!ix || (!d_q && nq) || !d_ids || !d_dists) return fail(RAVEN_EINVAL, "null argument");
   if (k == 0 || k > KMAXK) return fail(RAVEN_ELIMIT, "k must be in 1..32");
   if (nq == 0) return RAVEN_OK;
@@ -1269,6 +1284,7 @@ int raven_knn_exact_device(raven_index* ix, const float* d_q, uint64_t nq, uint3
 int raven_merge_topk_device(const uint32_t* d_ids, const float* d_dists, const uint32_t* d_counts, uint32_t n_shards,
                             uint64_t nq, uint32_t k, uint64_t shard_size, uint32_t* d_out_ids, float* d_out_dists,
                             uint32_t* d_out_counts, void* stream) {
+  NvtxRange nvtx_range("raven.merge_topk");
   if (!d_ids || !d_dists || !d_out_ids || !d_out_dists) return fail(RAVEN_EINVAL, "null argument");
   if (n_shards == 0 || k == 0) return fail(RAVEN_EINVAL, "n_shards and k must be >= 1");
   if (nq == 0) return RAVEN_OK;
@@ -1339,6 +1355,7 @@ extern "C" {
 
 int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
                                       const raven_search_outputs* o, void* stream) {
+  NvtxRange nvtx_range("raven.search_batch_device_noalloc");
   if (!ix) return fail(RAVEN_EINVAL, "null index");
   if (nq && !d_q) return fail(RAVEN_EINVAL, "null queries");
   Plan pl;
@@ -1680,6 +1697,7 @@ struct GpuBuild : raven::BuildAccelerator {
   }
   int search_prune(const uint32_t* nodes, size_t count, float alpha, std::vector<std::vector<uint32_t>>* pruned,
                    std::string* err) override {
+    NvtxRange nvtx_range("raven.build.search_prune");
     if (int e = ensure(count, err)) return e;
     const double t0 = now();
     cudaStream_t st = ix->stream;
@@ -1743,6 +1761,7 @@ struct GpuBuild : raven::BuildAccelerator {
     return 0;
   }
   int update_rows(const uint32_t* ids, size_t count, const uint32_t* main_block, std::string* err) override {
+    NvtxRange nvtx_range("raven.build.update_rows");
     if (count == 0) return 0;
     const double t0 = now();
     const uint32_t r = cfg.r_max;
@@ -1776,6 +1795,7 @@ extern "C" {
 
 int raven_graph_build_gpu(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg, int device,
                           raven_graph** out) {
+  NvtxRange nvtx_range("raven.graph_build_gpu");
   if (!out || (!vectors && n) || !cfg) return fail(RAVEN_EINVAL, "null argument");
   raven::BuildConfig c;
   c.alpha = cfg->alpha;
