@@ -1,0 +1,46 @@
+"""bench.py's reference arm runs on host cores only, so its JSON line can be
+checked here: the keys the benchmark contract names, a positive throughput,
+and the rule that under torchrun only rank 0 runs and prints (the other ranks
+exit 0 without work). Uses the small gmm100k-d128 workload (its graph is built
+on the host on first use and cached).
+"""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(extra_env=None, timeout=600):
+    env = dict(os.environ)
+    env.update(extra_env or {})
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "gmm100k-d128",
+           "--steps", "2", "--warmup", "1", "--batch", "600"]
+    return subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=timeout)
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = _run()
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+                "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["steps"] == 2 and line["warmup"] == 1 and line["n_gpus"] == 1
+    assert line["higher_is_better"] is True and line["unit"] == "queries/s"
+    assert line["value"] > 0 and line["ms_per_step"] > 0
+    assert "gmm100k-d128" in line["config"]["workload"] and line["config"]["ef"] == 50
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["value"] == line["value"] and cb["cores"] >= 1 and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_exit_silently():
+    r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""
