@@ -98,3 +98,39 @@ def test_upload_validates_ids_before_device_work(raven_lib):
     with pytest.raises(L.RavenError) as e:
         DeviceIndex(g2, np.zeros((3, 5), np.float32))
     assert e.value.code == L.RAVEN_EINVAL
+
+
+# ctypes mirror -> C typedef in include/raven_gpu.h
+_STRUCTS = {"BuildConfig": "raven_build_config", "GraphInfo": "raven_graph_info_t",
+            "UploadOptions": "raven_upload_options", "SearchParams": "raven_search_params",
+            "SearchOutputs": "raven_search_outputs", "Limits": "raven_limits_t"}
+
+
+def test_binding_structs_match_header_layout(tmp_path):
+    """Every ctypes struct has the C struct's size and each field's offset, as
+    compiled by gcc from the header (the layout a Rust #[repr(C)] mirror must
+    also have)."""
+    import shutil
+    import subprocess
+
+    from raven_b200 import _lib as L
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "raven_gpu.h"', "int main(void) {"]
+    for py, c in _STRUCTS.items():
+        lines.append(f'  printf("{py} size %zu\\n", sizeof({c}));')
+        for f, _ in getattr(L, py)._fields_:
+            lines.append(f'  printf("{py} {f} %zu\\n", offsetof({c}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {tuple(ln.split()[:2]): int(ln.split()[2]) for ln in out if ln.strip()}
+    for py in _STRUCTS:
+        cls = getattr(L, py)
+        assert got[(py, "size")] == C.sizeof(cls), py
+        for f, _ in cls._fields_:
+            assert got[(py, f)] == getattr(cls, f).offset, (py, f)
