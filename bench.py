@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-extras", action="store_true", help="skip the AdaptiveEf points and the 64-query latency run")
     ap.add_argument("--sweep", action="store_true", help="also report recall/QPS at other ef points")
     ap.add_argument("--hash-bits", type=int, default=0)
+    ap.add_argument("--spill-bits", type=int, default=0,
+                    help="log2 of the global visited-spill slots per warp (0 = automatic)")
     ap.add_argument("--shards", type=int, default=0,
                     help="split the workload into this many per-shard graphs (all-gather + merge across ranks)")
     ap.add_argument("--shard-n", type=int, default=0, help="vectors per shard (default: workload n / shards)")
@@ -421,8 +423,8 @@ def main():
     base, qbatches, g = load_workload(args, rank)
     quant = L.RAVEN_QUANT_SQ4 if args.quant == "sq4" else L.RAVEN_QUANT_SQ8
     dev = DeviceIndex(g, base, device=dev_id, sq4=quant == 0, sq8=quant == 1, adaptive=True)
-    if args.hash_bits:
-        dev.set_tuning(hash_bits=args.hash_bits)
+    if args.hash_bits or args.spill_bits:
+        dev.set_tuning(hash_bits=args.hash_bits, spill_bits=args.spill_bits)
     lib = L.load()
     nb, B, dim = qbatches.shape
     k = args.k
