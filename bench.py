@@ -156,11 +156,24 @@ def load_workload(args, rank):
     return base, np.stack(qs), g
 
 
-def cpu_baseline(args, base, g, queries, rank, budget_s=12.0):
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_baseline(args, base, g, queries, rank, budget_s=12.0, rounds=5):
     """The oracle (CPU restatement of the reference batch_search) on this
-    box's host cores, on a bounded sample of the same workload: passes over
-    the bench's query batches (wrapping around) sized to about `budget_s` of
-    host time."""
+    box's host cores, on a bounded sample of the same workload: after a
+    warm-up, `rounds` timed rounds with all host threads, each a pass over the
+    bench's query batches (wrapping around) sized so that the rounds take about
+    `budget_s` in total; the value is the median round's rate (the method of
+    the reference's ef sweep, src/bin/sq4_ef_sweep.rs:102-131). A one-thread
+    rate (median of 3 short rounds) is reported beside it."""
     import tempfile
 
     from oracle import oracle as O
@@ -173,24 +186,30 @@ def cpu_baseline(args, base, g, queries, rank, budget_s=12.0):
     threads = os.cpu_count() or 1
     q = queries.reshape(-1, queries.shape[-1])
     quant = 0 if args.quant == "sq4" else 1
-    oi.search(q[:256], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads)  # warm-up
-    n = 1024
-    t0 = time.perf_counter()
-    oi.search(q[:n], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads)
-    dt = time.perf_counter() - t0
-    # grow the sample to ~budget_s of wall time, wrapping around the batches
-    n2 = int(max(n, n * budget_s / max(dt, 1e-3)))
-    done = 0
-    t0 = time.perf_counter()
-    while done < n2:
-        s = done % q.shape[0]
-        m = min(q.shape[0] - s, n2 - done)
-        oi.search(q[s:s + m], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads)
-        done += m
-    dt = time.perf_counter() - t0
-    return {"value": n2 / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n2} queries of {args.workload} ({n2 / q.shape[0]:.1f} passes over its {q.shape[0]} "
-                      f"bench queries), ef={args.ef}, k={args.k}, rr={args.rr}, {threads} host threads, {dt:.2f} s"}
+    pos = [0]
+
+    def timed(n, th):
+        """Search the next n queries (wrapping around) on th threads; seconds."""
+        done = 0
+        t0 = time.perf_counter()
+        while done < n:
+            s = pos[0] % q.shape[0]
+            m = min(q.shape[0] - s, n - done)
+            oi.search(q[s:s + m], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=th)
+            done += m
+            pos[0] += m
+        return time.perf_counter() - t0
+
+    timed(256, threads)  # warm-up
+    probe = timed(1024, threads)
+    per_round = int(max(1024, 1024 * budget_s / rounds / max(probe, 1e-3)))
+    rates = sorted(per_round / timed(per_round, threads) for _ in range(rounds))
+    one = sorted(128 / timed(128, 1) for _ in range(3))
+    return {"value": rates[len(rates) // 2], "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"median of {rounds} rounds of {per_round} queries of {args.workload} (wrapping over its "
+                      f"{q.shape[0]} bench queries), ef={args.ef}, k={args.k}, rr={args.rr}, {threads} host threads",
+            "rounds_qps": [round(r, 1) for r in rates], "single_thread_qps": round(one[1], 1),
+            "cpu_model": cpu_model(), "nproc": threads}
 
 
 def run_reference(args):

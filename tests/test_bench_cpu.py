@@ -44,3 +44,25 @@ def test_reference_arm_other_ranks_exit_silently():
     r = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}, timeout=120)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_cpu_baseline_fields_and_bound():
+    """The CPU baseline of the GPU arm: median of its rounds, a one-thread rate,
+    the CPU model, and a wall time close to the budget it is given."""
+    import time
+    import types
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    args = types.SimpleNamespace(workload="gmm100k-d128", batch=1000, build_device=None, quant="sq4", k=10, ef=50,
+                                 rr=8)
+    base, qs, g = bench.load_workload(args, 0)
+    t0 = time.perf_counter()
+    cb = bench.cpu_baseline(args, base, g, qs, 0, budget_s=2.0, rounds=5)
+    wall = time.perf_counter() - t0
+    assert cb["kind"] == "port" and cb["unit"] == "queries/s" and cb["cores"] == cb["nproc"] >= 1
+    assert len(cb["rounds_qps"]) == 5 and cb["rounds_qps"] == sorted(cb["rounds_qps"])
+    assert cb["value"] > 0 and abs(cb["value"] - cb["rounds_qps"][2]) <= 0.05
+    assert cb["single_thread_qps"] > 0 and cb["cpu_model"]
+    assert wall < 30
