@@ -60,8 +60,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=10000)
     ap.add_argument("--quant", choices=["sq4", "sq8"], default="sq4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-extras", action="store_true", help="skip the AdaptiveEf points and the 64-query latency run")
-    ap.add_argument("--sweep", action="store_true", help="also report recall/QPS at other ef points")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the ef sweep, the AdaptiveEf points and the 64-query latency run")
+    ap.add_argument("--sweep", action="store_true", help="report the ef sweep even with --no-extras")
     ap.add_argument("--hash-bits", type=int, default=0)
     ap.add_argument("--spill-bits", type=int, default=0,
                     help="log2 of the global visited-spill slots per warp (0 = automatic)")
@@ -553,7 +554,7 @@ def main():
     e2e_value = e2e_steps * B * world / e2e_s
 
     sweep = None
-    if args.sweep and rank == 0:
+    if (args.sweep or not args.no_extras) and rank == 0:
         sweep = {}
         for ef in SWEEP_EFS:
             p2 = L.SearchParams(ef=ef, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=0,
