@@ -15,7 +15,10 @@
  * on one GPU. Threading: a raven_graph is immutable after load/build; a
  * raven_index is immutable after upload, and concurrent searches on distinct
  * CUDA streams are allowed (each call uses its own work counter; the
- * visited-set spill area is per call, see raven_search_batch_device).
+ * visited-set spill area is per call, see raven_search_batch_device). Two
+ * exceptions: raven_index_set_tuning changes the index and must not overlap a
+ * search call on it, and raven_search_batch_device_noalloc calls share one
+ * scratch array per GPU (see there).
  */
 #ifndef RAVEN_GPU_H
 #define RAVEN_GPU_H
