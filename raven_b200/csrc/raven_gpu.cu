@@ -543,7 +543,7 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   uint32_t hb = ix->hash_bits_override;
   if (hb == 0) {
     // Shared-memory visited slots per warp. Past 3/4 load a query continues
-    // in its global (L2-resident) spill table, whose probes overlap the code
+    // in its global spill table, whose probes overlap the code
     // gather; a smaller shared table buys residency. Measured on a 1M-node
     // graph: 2048 slots best at ef <= 64, 1024 beyond.
     hb = ef_cap <= 64 ? 11 : 10;

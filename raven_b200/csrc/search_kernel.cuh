@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
   const uint32_t pool_cap = POOLMAX ? (uint32_t)POOLMAX : a.pool_cap;
   const WarpSmem s = carve(smem_raw + (size_t)wib * a.smem_per_warp, a, pool_cap);
   const uint32_t slot = blockIdx.x * kWarpsPerBlock + wib;
-  // level A tables are contiguous (hot, L2/TLB friendly); level B only for outliers
+  // level A tables are contiguous (TLB friendly); level B only for outliers
   uint32_t* spill = a.spill ? a.spill + ((size_t)slot << a.spill_bits) : nullptr;
   uint32_t* spill_b = a.spill ? a.spill + (a.n_slots << a.spill_bits) + ((size_t)slot << (a.spill_bits + 3)) : nullptr;
   const uint32_t H = 1u << a.hash_bits;
