@@ -45,6 +45,7 @@ N_BATCHES = 4  # distinct 10k-query batches rotated across steps
 # Gaussian-mixture stand-in with a random 30% zero mask is harder.
 OPERATING_EF = {"gmm100k-d128": 50, "gmm1m-d128-sparse": 140}
 SWEEP_EFS = (40, 45, 50, 55, 65, 80, 100, 120, 140, 160, 200)
+PREFETCH_OFFSET = 8  # with_prefetch_offset of the measured configurations (po=8)
 
 
 def parse():
@@ -196,7 +197,8 @@ def cpu_baseline(args, base, g, queries, rank, budget_s=12.0, rounds=5):
         while done < n:
             s = pos[0] % q.shape[0]
             m = min(q.shape[0] - s, n - done)
-            oi.search(q[s:s + m], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=th)
+            oi.search(q[s:s + m], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=th,
+                      prefetch_offset=PREFETCH_OFFSET)
             done += m
             pos[0] += m
         return time.perf_counter() - t0
@@ -238,11 +240,13 @@ def run_reference(args):
     per_step = 256
     for w in range(args.warmup):
         s = (w * per_step) % (queries.shape[0] - per_step)
-        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads)
+        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
+                  prefetch_offset=PREFETCH_OFFSET)
     t0 = time.perf_counter()
     for st in range(args.steps):
         s = (st * per_step) % (queries.shape[0] - per_step)
-        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads)
+        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
+                  prefetch_offset=PREFETCH_OFFSET)
     dt = time.perf_counter() - t0
     qps = args.steps * per_step / dt
     line = {

@@ -26,6 +26,8 @@
 #include <thread>
 #include <vector>
 
+#include <xmmintrin.h>
+
 namespace {
 
 constexpr uint32_t kSentinel = 0xFFFFFFFFu;             // src/lib.rs:37
@@ -565,15 +567,27 @@ size_t estimate_ef(const std::vector<float>& s, size_t min_ef, size_t max_ef, fl
 
 // ---------------------------------------------------------------------------
 // greedy_search_sq4 / greedy_search_sq8::<true> — src/graph/vamana.rs:786-861
-// and :683-773 (prefetches have no semantic effect and are omitted).
+// and :683-773, with the reference's software prefetches (no effect on
+// results; kept so that the timed CPU baseline has the reference's memory
+// behaviour): the next unexpanded node's adjacency lines after each pop
+// (:808-819), the codes of the first `po` new neighbours (:834-842), and the
+// code `po` ahead of each distance (:846-853). `code_lines` code lines are
+// prefetched per neighbour (SQ4 1, SQ8 2), all with the NTA hint
+// (`_mm_prefetch::<0>`).
 // ---------------------------------------------------------------------------
 struct SearchStats {
   uint32_t expansions = 0;
 };
-template <class DistFn>
+template <class DistFn, class CodeFn>
 std::vector<std::pair<uint32_t, float>> greedy_search_q(const Index& ix, uint32_t entry, size_t l,
                                                         Visited& visited, LinearPool& pool,
-                                                        DistFn dist, SearchStats* st) {
+                                                        DistFn dist, CodeFn code_ptr, int code_lines, size_t po,
+                                                        SearchStats* st) {
+  auto prefetch_code = [&](uint32_t v) {
+    const char* c = (const char*)code_ptr(v);
+    for (int li = 0; li < code_lines; ++li) _mm_prefetch(c + 64 * li, _MM_HINT_NTA);
+  };
+  const size_t graph_lines = ((size_t)ix.r_max * 4 + 63) / 64;
   visited.reset();
   pool.reset_for(l);
   float ed = dist(entry);
@@ -584,6 +598,11 @@ std::vector<std::pair<uint32_t, float>> greedy_search_q(const Index& ix, uint32_
   float nd;
   while (pool.pop(&node, &nd)) {
     if (st) st->expansions++;
+    if (pool.has_next()) {  // peek_unchecked
+      const uint32_t next = pool.data[pool.cursor].first & ~kChecked;
+      const char* g = (const char*)(ix.main_block.data() + (size_t)next * ix.r_max);
+      for (size_t li = 0; li < graph_lines; ++li) _mm_prefetch(g + 64 * li, _MM_HINT_NTA);
+    }
     const uint32_t* nb = ix.main_block.data() + (size_t)node * ix.r_max;
     size_t deg = ix.degrees[node];
     size_t edge_size = 0;
@@ -594,7 +613,11 @@ std::vector<std::pair<uint32_t, float>> greedy_search_q(const Index& ix, uint32_
       edge_buf[edge_size] = v;
       edge_size += is_new ? 1 : 0;
     }
-    for (size_t i = 0; i < edge_size; ++i) pool.insert(edge_buf[i], dist(edge_buf[i]));  // :846-857
+    for (size_t i = 0; i < std::min(po, edge_size); ++i) prefetch_code(edge_buf[i]);
+    for (size_t i = 0; i < edge_size; ++i) {  // :846-857
+      if (i + po < edge_size) prefetch_code(edge_buf[i + po]);
+      pool.insert(edge_buf[i], dist(edge_buf[i]));
+    }
   }
   std::vector<std::pair<uint32_t, float>> out(pool.size);
   for (size_t i = 0; i < pool.size; ++i) out[i] = {pool.data[i].first & ~kChecked, pool.data[i].second};
@@ -641,6 +664,7 @@ struct OracleParams {
   float gamma;
   uint32_t min_ef, max_ef;
   uint32_t rerank_f16;  // 1: GraphSearcher::with_f16 (src/graph/vamana.rs:1559, 1824-1828)
+  uint32_t prefetch_offset;  // with_prefetch_offset (:1541); GraphSearcher::new sets 16 (:1490)
 };
 
 struct QueryOut {
@@ -692,11 +716,15 @@ int search_one(const Index& ix, const float* q, const OracleParams& p, Worker& w
   const uint8_t* qc = w.code.data();
   if (p.quant == 0) {
     const size_t cb = ix.sq4_bytes;
-    cands = greedy_search_q(ix, entry, ef, w.visited, w.pool,
-                            [&](uint32_t id) { return l2_sq4_raw(qc, ix.sq4_codes.data() + (size_t)id * cb, cb); }, &st);
+    cands = greedy_search_q(
+        ix, entry, ef, w.visited, w.pool,
+        [&](uint32_t id) { return l2_sq4_raw(qc, ix.sq4_codes.data() + (size_t)id * cb, cb); },
+        [&](uint32_t id) { return ix.sq4_codes.data() + (size_t)id * cb; }, 1, p.prefetch_offset, &st);
   } else {
-    cands = greedy_search_q(ix, entry, ef, w.visited, w.pool,
-                            [&](uint32_t id) { return l2_sq8_raw(qc, ix.sq8_codes.data() + (size_t)id * dim, dim); }, &st);
+    cands = greedy_search_q(
+        ix, entry, ef, w.visited, w.pool,
+        [&](uint32_t id) { return l2_sq8_raw(qc, ix.sq8_codes.data() + (size_t)id * dim, dim); },
+        [&](uint32_t id) { return ix.sq8_codes.data() + (size_t)id * dim; }, 2, p.prefetch_offset, &st);
   }
   out->visited = (uint32_t)w.visited.history.size();
   out->ef_used = (uint32_t)ef;

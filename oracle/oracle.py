@@ -22,7 +22,7 @@ u8p = C.POINTER(C.c_uint8)
 class OracleParams(C.Structure):
     _fields_ = [("ef", C.c_uint32), ("k", C.c_uint32), ("rerank_factor", C.c_uint32), ("quant", C.c_uint32),
                 ("adaptive", C.c_uint32), ("gamma", C.c_float), ("min_ef", C.c_uint32), ("max_ef", C.c_uint32),
-                ("rerank_f16", C.c_uint32)]
+                ("rerank_f16", C.c_uint32), ("prefetch_offset", C.c_uint32)]
 
 
 _SIG = {
@@ -289,11 +289,12 @@ class OracleIndex:
         return int(e.value), float(d.value), int(n.value)
 
     def search(self, queries, k=10, ef=50, rerank_factor=5, quant=0, adaptive=False, gamma=2.0, min_ef=30,
-               max_ef=100, threads=0, history_cap=0, rerank_f16=False) -> dict:
+               max_ef=100, threads=0, history_cap=0, rerank_f16=False, prefetch_offset=16) -> dict:
         q = np.ascontiguousarray(np.atleast_2d(queries), np.float32)
         nq = q.shape[0]
         p = OracleParams(ef=ef, k=k, rerank_factor=rerank_factor, quant=quant, adaptive=int(adaptive), gamma=gamma,
-                         min_ef=min_ef, max_ef=max_ef, rerank_f16=int(rerank_f16))
+                         min_ef=min_ef, max_ef=max_ef, rerank_f16=int(rerank_f16),
+                         prefetch_offset=prefetch_offset)
         r = {"ids": np.zeros((nq, k), np.uint32), "dists": np.zeros((nq, k), np.float32),
              "counts": np.zeros(nq, np.uint32), "visited": np.zeros(nq, np.uint32),
              "ef_used": np.zeros(nq, np.uint32), "n_nav": np.zeros(nq, np.uint32),
