@@ -237,14 +237,16 @@ def run_reference(args):
     oi.set_vectors(base, sq4=args.quant == "sq4", sq8=args.quant == "sq8")
     threads = os.cpu_count() or 1
     quant = 0 if args.quant == "sq4" else 1
-    per_step = 256
+    # 1024 queries per step: thread start-up and the end-of-step tail stay small
+    per_step = min(1024, queries.shape[0])
+    span = queries.shape[0] - per_step + 1  # step offsets wrap within the batch
     for w in range(args.warmup):
-        s = (w * per_step) % (queries.shape[0] - per_step)
+        s = (w * per_step) % span
         oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
                   prefetch_offset=PREFETCH_OFFSET)
     t0 = time.perf_counter()
     for st in range(args.steps):
-        s = (st * per_step) % (queries.shape[0] - per_step)
+        s = (st * per_step) % span
         oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
                   prefetch_offset=PREFETCH_OFFSET)
     dt = time.perf_counter() - t0
