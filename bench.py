@@ -61,6 +61,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=10000)
     ap.add_argument("--quant", choices=["sq4", "sq8"], default="sq4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle parity check (outside the timed region)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the ef sweep, the AdaptiveEf points and the 64-query latency run")
     ap.add_argument("--sweep", action="store_true", help="report the ef sweep even with --no-extras")
@@ -215,7 +216,21 @@ def cpu_baseline(args, base, g, queries, rank, budget_s=12.0, rounds=5):
             "cpu_model": cpu_model(), "nproc": threads}
 
 
+def workload_desc(args, n, dim):
+    """The `config.workload` string both arms print for the same workload."""
+    return (f"{args.workload}: {n} x {dim} seeded Gaussian mixture (SIFT-1M shape stand-in), Vamana R=32 L=200 "
+            f"alpha=1.2 DirectionalPrune nav_m=32; {args.quant.upper()} ef={args.ef} k={args.k} rr={args.rr}; "
+            f"batch {args.batch} queries per step")
+
+
 def run_reference(args):
+    """The reference arm: the oracle port of GraphSearcher::batch_search (the
+    Rust reference cannot be built here) on this box's host cores, on the same
+    workload, index, query batches and search parameters as the engine's arm;
+    one step = one batch, the batches rotating as in the engine's arm. The
+    index is read with the oracle's own ANNX reader; if it is not cached, it is
+    built with the host build (oracle/_build/libhostbuild.so) and saved. The
+    engine's CUDA library is not loaded."""
     if args.ef is None:
         args.ef = OPERATING_EF.get(args.workload, 50)
     rank, world, local = dist_env()
@@ -226,46 +241,93 @@ def run_reference(args):
     from raven_b200 import datasets
 
     base, _ = datasets.make(args.workload, nq=1)
-    queries = datasets.make_queries(args.workload, args.batch, offset=0)
-    g = datasets.load_or_build(args.workload, base=base)
+    qb = np.stack([datasets.make_queries(args.workload, args.batch, offset=b) for b in range(N_BATCHES)])
+    path = datasets.index_path(args.workload)
+    t0 = time.time()
+    if not os.path.exists(path):
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        O.build_index_file(base, path + ".tmp")
+        os.replace(path + ".tmp", path)
+    oi = O.OracleIndex(path)
+    oi.set_vectors(base, sq4=args.quant == "sq4", sq8=args.quant == "sq8")
+    load_s = time.time() - t0
+    threads = os.cpu_count() or 1
+    quant = 0 if args.quant == "sq4" else 1
+
+    def step(i):
+        oi.search(qb[i % N_BATCHES], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
+                  prefetch_offset=PREFETCH_OFFSET)
+
+    for w in range(args.warmup):
+        step(w)
+    t0 = time.perf_counter()
+    for st in range(args.steps):
+        step(st)
+    dt = time.perf_counter() - t0
+    qps = args.steps * args.batch / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "sq4-int32+f32" if quant == 0 else "sq8-int32+f32",
+        "data": "synthetic (seeded Gaussian mixture with the SIFT-1M shape; no dataset download)",
+        "config": {"workload": workload_desc(args, base.shape[0], base.shape[1]), "ef": args.ef,
+                   "index": f"host-built or cached graph (oracle ANNX reader), loaded/built in {load_s:.1f} s"},
+        "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.batch} queries per step x {args.steps} steps ({N_BATCHES} batches "
+                                   f"rotating), {threads} host threads (C++ restatement of "
+                                   "GraphSearcher::batch_search; the Rust reference cannot be built here)",
+                         "cpu_model": cpu_model()},
+        "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def parity_check(args, g, base, dev, qbatches, n_check=1000):
+    """Checker, outside the timed region: the engine (raven_search_batch, the
+    public C ABI with host buffers) against the oracle on the first `n_check`
+    queries of batch 0, at the bench's ef and at ef=50, on every output:
+    top-k ids, result counts, visited counts, visited order, ef used,
+    navigation evaluations, expansions and the f32 rerank distances."""
     import tempfile
+
+    from oracle import oracle as O
+    from raven_b200 import _lib as L
 
     with tempfile.TemporaryDirectory() as d:
         p = os.path.join(d, "g.annx")
         g.save(p)
         oi = O.OracleIndex(p)
     oi.set_vectors(base, sq4=args.quant == "sq4", sq8=args.quant == "sq8")
-    threads = os.cpu_count() or 1
     quant = 0 if args.quant == "sq4" else 1
-    # 1024 queries per step: thread start-up and the end-of-step tail stay small
-    per_step = min(1024, queries.shape[0])
-    span = queries.shape[0] - per_step + 1  # step offsets wrap within the batch
-    for w in range(args.warmup):
-        s = (w * per_step) % span
-        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
-                  prefetch_offset=PREFETCH_OFFSET)
-    t0 = time.perf_counter()
-    for st in range(args.steps):
-        s = (st * per_step) % span
-        oi.search(queries[s:s + per_step], k=args.k, ef=args.ef, rerank_factor=args.rr, quant=quant, threads=threads,
-                  prefetch_offset=PREFETCH_OFFSET)
-    dt = time.perf_counter() - t0
-    qps = args.steps * per_step / dt
-    line = {
-        "impl": "reference", "metric": METRIC, "value": qps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "sq4-int32+f32" if quant == 0 else "sq8-int32+f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: SQ4 ef={args.ef} k={args.k} rr={args.rr} "
-                               "(ef = the workload's recall@10>=0.95 operating point)",
-                   "per_step_queries": per_step, "ef": args.ef},
-        "cpu_baseline": {"value": qps, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{per_step} queries per step x {args.steps} steps, {threads} host threads "
-                                   "(C++ restatement of GraphSearcher::batch_search; the Rust reference cannot be "
-                                   "built here)"},
-        "e2e": {"value": qps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    q = np.ascontiguousarray(qbatches[0][:n_check])
+    hist = 16384
+    res = {"queries": int(q.shape[0]), "efs": [], "ids_equal": True, "counts_equal": True, "visited_equal": True,
+           "history_equal": True, "stats_equal": True, "max_rel_dist_err": 0.0,
+           "oracle": "C++ restatement of the reference search (oracle/), pinned by the reference's known answers"}
+    for ef in sorted({args.ef, 50}):
+        params = L.SearchParams(ef=ef, k=args.k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=0,
+                                gamma=0.0, min_ef=0, max_ef=0)
+        got = dev.search(q, params, history_cap=hist)
+        exp = oi.search(q, k=args.k, ef=ef, rerank_factor=args.rr, quant=quant, history_cap=hist,
+                        threads=os.cpu_count() or 1)
+        res["efs"].append(ef)
+        res["ids_equal"] &= bool(np.array_equal(got["ids"], exp["ids"]))
+        res["counts_equal"] &= bool(np.array_equal(got["counts"], exp["counts"]))
+        res["visited_equal"] &= bool(np.array_equal(got["visited"], exp["visited"]))
+        res["stats_equal"] &= bool(all(np.array_equal(got[k], exp[k]) for k in ("ef_used", "n_nav", "expansions")))
+        h_ok = bool(np.array_equal(got["history_len"], exp["history_len"]))
+        if h_ok:
+            for i in range(q.shape[0]):
+                h = min(int(got["history_len"][i]), hist)
+                if not np.array_equal(got["history"][i, :h], exp["history"][i, :h]):
+                    h_ok = False
+                    break
+        res["history_equal"] &= h_ok
+        den = np.maximum(np.abs(exp["dists"]), 1e-30)
+        res["max_rel_dist_err"] = max(res["max_rel_dist_err"], float(np.max(np.abs(got["dists"] - exp["dists"]) / den)))
+        res["bad_status"] = int(np.sum(got["status"] != 0))
+    return res
 
 
 def run_sharded(args):
@@ -643,6 +705,13 @@ def main():
             lat[name] = {"p50_us": round(ts[len(ts) // 2], 1), "p99_us": round(ts[int(len(ts) * 0.99)], 1)}
         latency = {"queries_per_launch": lat_q, "launches": lat_n, "device_time_per_launch": lat}
 
+    parity = None
+    if rank == 0 and not args.no_parity:
+        try:
+            parity = parity_check(args, g, base, dev, qbatches)
+        except Exception as e:  # reported in the line, never silently dropped
+            parity = {"error": f"{type(e).__name__}: {e}"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -658,12 +727,11 @@ def main():
         "dtype": "sq4-int32+f32" if quant == 0 else "sq8-int32+f32",
         "data": "synthetic (seeded Gaussian mixture with the SIFT-1M shape; no dataset download)",
         "config": {
-            "workload": f"{args.workload}: {base.shape[0]} x {dim} seeded Gaussian mixture "
-                        f"(SIFT-1M shape stand-in), Vamana R=32 L=200 alpha=1.2 DirectionalPrune nav_m=32; "
-                        f"SQ4 ef={args.ef} k={k} rr={args.rr}; batch {B} queries per step",
+            "workload": workload_desc(args, base.shape[0], dim),
             "ef": args.ef, "ef_choice": "smallest ef with recall@10 >= 0.95 on this workload "
                                         "(the reference reaches 0.95 at ef=50 on SIFT-1M)",
             "ef50_point": ef50,
+            "parity": parity,
             "recall_at_10": round(recall, 4), "queries_scored": int(got.shape[0]),
             "bad_status_queries": bad_status,
             "avg_visited": float(st["visited"].mean()), "avg_expansions": float(st["expansions"].mean()),

@@ -187,8 +187,9 @@ RAVEN_API int raven_search_batch_device(raven_index* ix, const float* d_queries,
  * device array that every GPU loading this library holds until the process
  * exits, instead of the stream-ordered pool used by raven_search_batch_device.
  * Same inputs, outputs and results. The first call on a device looks up that
- * array's device address (cudaGetSymbolAddress); make that first call before any
- * stream capture. All calls share the array: calls that overlap on the GPU
+ * array's device address (cudaGetSymbolAddress), as does the first call after
+ * the device's context was replaced (cudaDeviceReset); make those calls before
+ * any stream capture. All calls share the array: calls that overlap on the GPU
  * (e.g. on two streams) race and must be serialised by the caller. To fit the
  * array, spill tables are smaller (each query can still hold over 14,000 visited
  * nodes before reporting RAVEN_Q_VISITED_OVERFLOW) and fewer warps may be
@@ -200,7 +201,10 @@ RAVEN_API int raven_search_batch_device_noalloc(raven_index* ix, const float* d_
 
 /* Exact k-nearest neighbours over the uploaded f32 vectors (recall ground
  * truth; no reference counterpart — the reference reads SIFT groundtruth
- * files, src/bin/sq4_ef_sweep.rs:61). Device buffers; ties broken by id. */
+ * files, src/bin/sq4_ef_sweep.rs:61). Device buffers; ties broken by id.
+ * Every wait inside the tensor-core kernel is bounded: if one runs out, the
+ * call returns RAVEN_ECUDA and its outputs are not valid, and the kernel lets
+ * its own copies and MMAs finish before it frees tensor memory and exits. */
 RAVEN_API int raven_knn_exact_device(raven_index* ix, const float* d_queries, uint64_t nq, uint32_t k, uint32_t* d_ids,
                            float* d_dists, void* stream);
 

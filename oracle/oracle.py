@@ -344,3 +344,27 @@ def merge_shard_lists(ids, dists, counts, shard_size, k):
             out_i[qi, r] = s * shard_size + int(ids[s, qi, rr])
         out_c[qi] = min(len(c), k)
     return out_i, out_d, out_c
+
+
+HOSTBUILD_LIB = os.path.join(HERE, "_build", "libhostbuild.so")
+
+
+def build_index_file(vectors, path, r=32, l=200, alpha=1.2, nav_m=32, directional=True, r_soft=None,
+                     max_iterations=2, seed=42, threads=0) -> None:
+    """Build the Vamana index of `vectors` on the host (the C++ restatement of
+    the reference's offline pipeline, PyO3 build parameters by default) and
+    write it to `path` as an ANNX v1 file, through oracle/_build/libhostbuild.so
+    (the engine's CUDA library is not loaded)."""
+    if not os.path.exists(HOSTBUILD_LIB):
+        build()
+    hb = C.CDLL(HOSTBUILD_LIB)
+    f = hb.hostbuild_build_save
+    f.restype = C.c_int
+    f.argtypes = [f32p, C.c_ulonglong, C.c_uint, C.c_float, C.c_uint, C.c_uint, C.c_uint, C.c_uint, C.c_int,
+                  C.c_uint, C.c_ulonglong, C.c_int, C.c_char_p, C.c_char_p, C.c_size_t]
+    v = np.ascontiguousarray(vectors, np.float32)
+    err = C.create_string_buffer(512)
+    rc = f(_p(v, C.c_float), v.shape[0], v.shape[1], alpha, l, r, int(r * 1.5) if r_soft is None else r_soft,
+           max_iterations, int(directional), nav_m, seed, threads, os.fsencode(path), err, len(err))
+    if rc != 0:
+        raise RuntimeError(f"host build failed ({rc}): {err.value.decode()}")

@@ -296,21 +296,35 @@ struct Rng {
   double uniform() { return (double)(next() >> 11) * (1.0 / 9007199254740992.0); }
 };
 
+// l2_simd as the reference computes it on AVX-512 hardware
+// (src/distance/avx512.rs:31-62): 16 lane chains of fused multiply-adds over
+// the full 16-element blocks, each halving-tree reduced (_mm512_reduce_add_ps:
+// lanes j and j+8, then +4, +2, +1), the masked tail as its own vector reduced
+// the same way, result = tail + main. The same order as the GPU kernels'
+// distances, so host and GPU builds take the same decisions on float data.
+inline float tree16(float (&v)[16]) {
+  for (int w = 8; w >= 1; w >>= 1)
+    for (int j = 0; j < w; ++j) v[j] = v[j] + v[j + w];
+  return v[0];
+}
 inline float l2(const float* a, const float* b, size_t d) {
   float acc[16] = {0};
   size_t i = 0;
   for (; i + 16 <= d; i += 16)
     for (int j = 0; j < 16; ++j) {
-      float t = a[i + j] - b[i + j];
-      acc[j] += t * t;
+      const float t = a[i + j] - b[i + j];
+      acc[j] = std::fma(t, t, acc[j]);
     }
-  float s = 0;
-  for (; i < d; ++i) {
-    float t = a[i] - b[i];
-    s += t * t;
+  float result = 0.0f;
+  if (i < d) {
+    float tail[16] = {0};
+    for (size_t j = 0; i + j < d; ++j) {
+      const float t = a[i + j] - b[i + j];
+      tail[j] = std::fma(t, t, 0.0f);
+    }
+    result = tree16(tail);
   }
-  for (int j = 0; j < 16; ++j) s += acc[j];
-  return s;
+  return result + tree16(acc);
 }
 
 // HybridBlockedCsr mutators (src/memory/graph.rs:114-170).

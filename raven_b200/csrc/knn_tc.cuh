@@ -20,7 +20,10 @@
 // the epilogue: thread r owns query r of the tile (tensor-memory lane r),
 // reads its 128 dot products per base tile and keeps a sorted top-k in
 // registers (ties by id). Every mbarrier wait is bounded; a wait that runs out
-// sets an error flag and the kernel drains and returns.
+// sets an error flag. Before the tensor memory is freed and the CTA exits, the
+// producer waits for every TMA load it issued to land and the MMA issuer for
+// every MMA it issued to complete (both bounded), so no copy or MMA of this CTA
+// can write into shared or tensor memory that a later CTA is given.
 #pragma once
 
 #include <cuda.h>
@@ -47,8 +50,8 @@ struct Layout {
   static constexpr uint32_t kA = 0;                   // query blocks: [part][kb]
   static constexpr uint32_t kB = kParts * kMaxKB * kBlockBytes;
   static constexpr uint32_t kBars = kB + kStages * kParts * kBlockBytes;
-  // barriers: a_full, full[S], empty[S], acc_full[2], acc_empty[2]; then the tmem slot
-  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 4;
+  // barriers: a_full, full[S], empty[S], acc_full[2], acc_empty[2], drain; then the tmem slot
+  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 5;
   static constexpr uint32_t kTmemSlot = kBars + kNumBars * 8;
   static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;  // + alignment slack
 };
@@ -200,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto empty = [&](int s) { return bar0 + 8u * (1 + S + s); };
   auto acc_full = [&](int b) { return bar0 + 8u * (1 + 2 * S + b); };
   auto acc_empty = [&](int b) { return bar0 + 8u * (3 + 2 * S + b); };
+  const uint32_t drain = bar0 + 8u * (5 + 2 * S);  // completion of every MMA this CTA issued
   auto a_blk = [&](int part, int kb) { return sbase + L::kA + (uint32_t)(part * kMaxKB + kb) * kBlockBytes; };
   auto b_blk = [&](int s, int part) { return sbase + L::kB + (uint32_t)(s * L::kParts + part) * kBlockBytes; };
   uint32_t* tmem_slot = (uint32_t*)(smem + L::kTmemSlot);
@@ -222,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), kEpiWarps);  // one arrive per epilogue warp
     }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 2) {
@@ -245,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int s = 0;
       uint32_t ph = 0;
+      uint32_t used = 0, last_ph = 0;  // bit s: stage s was loaded; its last load's phase parity
       for (uint32_t t = 0; t < ntiles && ok; ++t) {
         const int row = (int)(r_begin + (uint64_t)t * kBN);
         for (uint32_t kb = 0; kb < KB; ++kb) {
@@ -255,12 +261,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(full(s), kBlockBytes * L::kParts);
           tma_load_2d(b_blk(s, 0), &tm_xh, (int)(kb * kBK), row, full(s));
           if (PASSES == 3) tma_load_2d(b_blk(s, 1), &tm_xl, (int)(kb * kBK), row, full(s));
+          used |= 1u << s;
+          last_ph = (last_ph & ~(1u << s)) | (ph << s);
           if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
         }
       }
+      // drain: every load issued has landed (immediate unless a wait ran out)
+      bool landed = mbar_wait(a_full, 0);
+#pragma unroll
+      for (int st = 0; st < S; ++st)
+        if ((used >> st) & 1u) landed &= mbar_wait(full(st), (last_ph >> st) & 1u);
+      ok &= landed;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
@@ -301,6 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) mma_commit(acc_full(b));
       }
+      // drain: every MMA issued has completed (immediate unless a wait ran out)
+      mma_commit(drain);
+      ok &= mbar_wait(drain, 0);
     }
   } else if (warp >= 4) {
     // epilogue: warp w reads tensor-memory lanes 32*(w%4).. (query rows) and

@@ -1333,28 +1333,55 @@ int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bit
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB per GPU
-constexpr size_t kNoAllocHeader = 16384;               // counter + ef table (<= 2001 u32)
+constexpr size_t kNoAllocHeader = 16384;               // counter (256 B) + ef table (<= 4032 u32)
 constexpr uint32_t kNoAllocMaxSpillBits = 11;          // spill level A 8 KB, level B 64 KB per warp
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// The CUDA context current on the calling thread (driver entry point looked up
+// once through the runtime; null if it is unavailable).
+void* current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuCtxGetCurrent_v4000)p;
+    else
+      (void)cudaGetLastError();
+  });
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return (void*)c;
+}
+
 std::mutex g_noalloc_mu;
-uint8_t* g_noalloc_ptr[256] = {};  // device address of g_noalloc_scratch, per device ordinal
+struct NoAllocSlot {
+  void* ctx = nullptr;    // context the address was taken in
+  uint8_t* ptr = nullptr;  // device address of g_noalloc_scratch in that context
+};
+NoAllocSlot g_noalloc_slot[256];  // per device ordinal
 
 // In host code g_noalloc_scratch names a host-side stand-in, not device memory:
-// the device address comes from cudaGetSymbolAddress, once per device, with
-// that device current.
+// the device address comes from cudaGetSymbolAddress, taken once per device
+// with that device current, and taken again if the device's context has been
+// replaced since (cudaDeviceReset destroys the array with its context).
 int noalloc_scratch(int device, uint8_t** out) {
   if (device < 0 || device >= 256) return fail(RAVEN_EINVAL, "device ordinal out of range");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[device]) {
+  NoAllocSlot& sl = g_noalloc_slot[device];
+  void* ctx = current_context();
+  if (!sl.ptr || ctx != sl.ctx) {
     void* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || ptr == nullptr)
       return fail(RAVEN_ECUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
-    g_noalloc_ptr[device] = (uint8_t*)ptr;
+    sl.ptr = (uint8_t*)ptr;
+    sl.ctx = current_context();  // the lookup may have created the primary context
   }
-  *out = g_noalloc_ptr[device];
+  *out = sl.ptr;
   return RAVEN_OK;
 }
 

@@ -2,9 +2,11 @@
 
 The known answers in reference_kat.json were transcribed from the reference's
 #[test] functions (it is Rust and cannot be built here). When the reference
-tree is available (REF_ROOT, default /root/reference) this script re-reads
-each cited test and asserts that the constants in the JSON occur in it, so a
-transcription error is caught. Usage:  python tests/golden/make_kat.py
+tree is available this script re-reads each cited test and asserts that the
+constants in the JSON occur in it, so a transcription error is caught. The
+tree's location is required, as the first argument or the REF_ROOT variable:
+
+    python tests/golden/make_kat.py <reference source tree>
 """
 from __future__ import annotations
 
@@ -14,7 +16,6 @@ import re
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("REF_ROOT", "/root/reference")
 
 # tokens that must appear in the cited line range of each case
 TOKENS = {
@@ -54,11 +55,15 @@ def cases(d, prefix=""):
             yield from cases(v, prefix + k + ".")
 
 
-def main() -> int:
+def main(argv) -> int:
+    REF = argv[1] if len(argv) > 1 else os.environ.get("REF_ROOT")
+    if not REF:
+        print("usage: make_kat.py <reference source tree>  (or set REF_ROOT)")
+        return 2
     kat = json.load(open(os.path.join(HERE, "reference_kat.json")))
     if not os.path.isdir(REF):
-        print(f"reference tree not found at {REF}; nothing to check")
-        return 0
+        print(f"reference tree not found at {REF}")
+        return 2
     bad = 0
     for name, c in cases(kat):
         m = re.match(r"(.+):(\d+)-(\d+)", c["source"])
@@ -74,4 +79,4 @@ def main() -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main())
+    sys.exit(main(sys.argv))

@@ -134,3 +134,17 @@ def test_binding_structs_match_header_layout(tmp_path):
         assert got[(py, "size")] == C.sizeof(cls), py
         for f, _ in cls._fields_:
             assert got[(py, f)] == getattr(cls, f).offset, (py, f)
+
+
+def test_raven_import_name():
+    """`import raven` gives the PyO3 module's two classes (src/python.rs:355-360)
+    with the reference's constructor defaults and errors."""
+    import raven
+
+    assert set(raven.__all__) == {"Index", "Searcher"}
+    ix = raven.Index("L2", 64)
+    assert (ix.r, ix.l, ix.alpha, ix.nav_m, ix.quant, ix.rerank) == (32, 200, 1.2, 32, "sq8", 5)
+    with pytest.raises(ValueError):
+        raven.Index("L2", 64, quantization="pq")
+    with pytest.raises(RuntimeError):
+        ix.searcher()

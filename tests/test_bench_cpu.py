@@ -66,3 +66,24 @@ def test_cpu_baseline_fields_and_bound():
     assert cb["value"] > 0 and abs(cb["value"] - cb["rounds_qps"][2]) <= 0.05
     assert cb["single_thread_qps"] > 0 and cb["cpu_model"]
     assert wall < 30
+
+
+def test_reference_arm_never_loads_the_engine_library():
+    """The reference arm times the oracle port only: the engine's CUDA library
+    is never mapped into its process (the index is read by the oracle's own
+    ANNX reader and, when missing, built by oracle/_build/libhostbuild.so)."""
+    code = (
+        "import sys, io, contextlib\n"
+        f"sys.path.insert(0, {ROOT!r})\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'gmm100k-d128', '--steps', '1', '--warmup', '0',"
+        " '--batch', '200']\n"
+        "import bench\n"
+        "with contextlib.redirect_stdout(io.StringIO()):\n"
+        "    assert bench.main() == 0\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "assert 'liboracle.so' in maps\n"
+        "print('libraven_gpu.so' in maps)\n"
+    )
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip().splitlines()[-1] == "False"

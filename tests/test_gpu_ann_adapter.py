@@ -1,6 +1,6 @@
 """The call sequence of the ann-benchmarks adapter
-(ann_benchmarks/algorithms/raven/module.py:47-91) against this package used as
-`raven`: Index(..., adaptive_ef=True) -> build -> searcher(); fixed ef via
+(ann_benchmarks/algorithms/raven/module.py:47-91) against the `raven`
+package: Index(..., adaptive_ef=True) -> build -> searcher(); fixed ef via
 set_ef and AdaptiveEf via set_adaptive_ef; per-query search() and
 batch_search().reshape(-1, n). Single-query results equal the batch results,
 and both equal the oracle's search of the same index.
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_ann_benchmarks_call_sequence(raven_lib, oracle):
-    import raven_b200 as raven
+    import raven
     from raven_b200 import datasets
 
     base, q = datasets.make("gmm100k-d128", n=4000, nq=40)

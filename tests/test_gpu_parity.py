@@ -379,16 +379,16 @@ def test_gmm100k_full_parity(oracle, raven_lib):
 def test_gmm1m_headline_parity(oracle, raven_lib):
     """The headline 1M x 128 workload (SQ4, k=10, rr=8) at ef=50 and at its
     recall>=0.95 operating point ef=140: 2,000 queries compared with the oracle
-    on every output, and no query of a 10,000 batch hits a capacity limit."""
+    on every output, and no query of a 10,000 batch hits a capacity limit.
+    Without a cached index file the graph is built here with the GPU build
+    (about a minute) and cached; parity holds on whichever graph is searched."""
     from raven_b200 import datasets
     from raven_b200.index import DeviceIndex
 
     wl = "gmm1m-d128-sparse"
-    if not os.path.exists(datasets.index_path(wl)):
-        pytest.skip("cached 1M index file not present (build it with raven_b200.datasets.load_or_build)")
     base, _ = datasets.make(wl, nq=1)
     q = datasets.make_queries(wl, 10000)
-    g = datasets.load_or_build(wl, base=base)
+    g = datasets.load_or_build(wl, base=base, device=0)
     dev = DeviceIndex(g, base, sq4=True)
     oi = _oracle_for(oracle, g, base, sq8=False, adaptive=False)
     for ef in (50, 140):

@@ -2,7 +2,7 @@
 Gaussian base vectors, 10 queries, Index("L2", 64, r=16, l=100, alpha=1.2,
 nav_m=16, directional=True) with the default quantization, SQ8, and rerank
 factor 5; single-query and batch search; ef switched over 20/50/100; recall
-against brute force) through this package used as `raven`. Beyond the
+against brute force) through the `raven` package. Beyond the
 reference's printed recall: single and batch results are equal, both equal
 the oracle's search of the same index at every ef, and recall does not drop
 as ef grows.
@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_pybinding_scenario(raven_lib, oracle):
-    import raven_b200 as raven
+    import raven
 
     rng = np.random.default_rng(42)
     data = rng.standard_normal((1000, 64)).astype(np.float32)
