@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--quant", choices=["sq4", "sq8"], default="sq4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle parity check (outside the timed region)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the sharded-collection record (8 shards, all-gather + GPU merge) of the default line")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the ef sweep, the AdaptiveEf points and the 64-query latency run")
     ap.add_argument("--sweep", action="store_true", help="report the ef sweep even with --no-extras")
@@ -330,6 +332,153 @@ def parity_check(args, g, base, dev, qbatches, n_check=1000):
     return res
 
 
+SHARDED_N = 8  # shards of the sharded-collection record in the default line
+
+
+def _shard_graph(args, part, s, S, shard_n, world, local):
+    """The cached graph of shard s, or a GPU build of it (saved for later runs)."""
+    from raven_b200 import datasets
+    from raven_b200.index import Graph
+
+    path = datasets.shard_index_path(args.workload, s, S, shard_n)
+    if os.path.exists(path):
+        return Graph.load(path), path
+    # torchrun sets OMP_NUM_THREADS=1: give each rank's host part of the build
+    # its share of the cores explicitly
+    g = Graph.build(part, r=32, l=200, alpha=1.2, nav_m=32, directional=True, seed=42 + s,
+                    threads=max(1, (os.cpu_count() or 1) // world), device=local)
+    os.makedirs(os.path.dirname(path), exist_ok=True)
+    g.save(path + f".tmp{os.getpid()}")
+    os.replace(path + f".tmp{os.getpid()}", path)
+    return g, path
+
+
+def sharded_record(args, base, world, rank, local, steps, n_shards=SHARDED_N, n_check=200):
+    """The sharded-collection layout at this N (every rank takes part): the
+    workload's base vectors split into `n_shards` contiguous shards, each with
+    its own Vamana graph (GPU build, f32 candidate search) and SQ4 codes,
+    shard s on rank s % N; a step = one batch searched on every shard (SQ4,
+    ef=50, k, rr), the per-shard lists all-gathered over NCCL and merged on
+    the GPU. Device-timed (max over ranks) with the step's split into search,
+    exchange and merge; e2e through the same call with the batch copied from
+    pinned host memory and the merged ids copied back every step; recall
+    against the exact top-k of the whole collection (exact kNN per shard,
+    merged the same way); and a check that the merged lists equal the
+    reference's per-shard searches (the oracle) merged on the host."""
+    import torch
+    import torch.distributed as tdist
+
+    from oracle import oracle as O
+    from raven_b200 import _lib as L
+    from raven_b200 import datasets
+    from raven_b200 import multigpu as M
+    from raven_b200.index import DeviceIndex
+
+    dist_on = world > 1
+    S, n, k, B = n_shards, base.shape[0], args.k, args.batch
+    shard_n = n // S
+    mine = M.shards_of_rank(S, world, rank)
+    t0 = time.time()
+    shards, paths, parts = {}, {}, {}
+    for s in mine:
+        parts[s] = np.ascontiguousarray(base[s * shard_n:(s + 1) * shard_n])
+        g, paths[s] = _shard_graph(args, parts[s], s, S, shard_n, world, local)
+        shards[s] = DeviceIndex(g, parts[s], device=local, sq4=True)
+    build_s = time.time() - t0
+    coll = M.ShardedCollection(shards, S, shard_n)
+    qb = np.stack([datasets.make_queries(args.workload, B, offset=b) for b in range(N_BATCHES)])
+    d_q = torch.from_numpy(qb).cuda()
+    params = L.SearchParams(ef=50, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=L.RAVEN_QUANT_SQ4,
+                            adaptive=0, gamma=0.0, min_ef=0, max_ef=0)
+    stream = torch.cuda.Stream()
+    truth = []
+    for b in range(N_BATCHES):
+        ti, _, _ = coll.exact(d_q[b], k, stream)
+        stream.synchronize()
+        truth.append(ti.cpu().numpy().view(np.uint32))
+    for i in range(max(3, N_BATCHES)):
+        coll.search(d_q[i % N_BATCHES], params, stream)
+    stream.synchronize()
+    rec = []
+    for b in range(N_BATCHES):
+        ids, _, _ = coll.search(d_q[b], params, stream)
+        stream.synchronize()
+        got = ids.cpu().numpy().view(np.uint32)
+        rec += [len(set(got[i]) & set(truth[b][i])) / k for i in range(B)]
+    # timed region: `steps` steps, events around each phase
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    if dist_on:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        ev[i][0].record(stream)
+        coll.search(d_q[i % N_BATCHES], params, stream, marks=(ev[i][1], ev[i][2]))
+        ev[i][3].record(stream)
+    torch.cuda.synchronize()
+    tot = sum(e[0].elapsed_time(e[3]) for e in ev)
+    t_search = sum(e[0].elapsed_time(e[1]) for e in ev)
+    t_xchg = sum(e[1].elapsed_time(e[2]) for e in ev)
+    t_merge = sum(e[2].elapsed_time(e[3]) for e in ev)
+    ms = M.max_over_ranks(tot, device=torch.device("cuda", local))
+    xchg_max = M.max_over_ranks(t_xchg, device=torch.device("cuda", local))
+    # e2e: batch from pinned host memory, merged ids back to the host, every step
+    hq = torch.from_numpy(qb).pin_memory()
+    h_ids = torch.zeros((B, k), dtype=torch.int32).pin_memory()
+    e2e_steps = max(5, steps // 4)
+    if dist_on:
+        tdist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            dq = hq[i % N_BATCHES].to("cuda", non_blocking=True)
+        ids, _, _ = coll.search(dq, params, stream)
+        with torch.cuda.stream(stream):
+            h_ids.copy_(ids, non_blocking=True)
+        stream.synchronize()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = M.max_over_ranks(f0.elapsed_time(f1), device=torch.device("cuda", local))
+    # parity: this rank's shard lists against the oracle's search of each shard;
+    # rank 0: the merge of the gathered lists against the host merge rule
+    ok = True
+    q = np.ascontiguousarray(qb[0][:n_check])
+    for s in mine:
+        oi = O.OracleIndex(paths[s])
+        oi.set_vectors(parts[s], sq4=True)
+        exp = oi.search(q, k=k, ef=50, rerank_factor=args.rr, threads=max(1, (os.cpu_count() or 1) // world))
+        got = shards[s].search(q, params)
+        ok &= all(np.array_equal(got[f], exp[f]) for f in ("ids", "dists", "counts", "visited"))
+    ids, _, cnt = coll.search(d_q[0], params, stream)
+    stream.synchronize()
+    gi, gd, gc = M.read_gathered(coll.gathered(B, k, d_q.device), S, world, B, k)
+    if rank == 0:
+        wi, wd, wc = O.merge_shard_lists(gi[:, :n_check], gd[:, :n_check], gc[:, :n_check], shard_n, k)
+        ok &= bool(np.array_equal(ids.cpu().numpy().view(np.uint32)[:n_check], wi) and
+                   np.array_equal(cnt.cpu().numpy().view(np.uint32)[:n_check], wc))
+    ok_all = M.max_over_ranks(0.0 if ok else 1.0, device=torch.device("cuda", local)) == 0.0
+    rec_mean = float(np.mean(rec))
+    del coll, shards
+    return {
+        "layout": f"{args.workload} split into {S} contiguous shards of {shard_n}, each its own Vamana graph "
+                  f"(R=32 L=200 alpha=1.2 DirectionalPrune nav_m=32, GPU build) and SQ4 codes; shard s on rank "
+                  f"s % {world}; SQ4 ef=50 k={k} rr={args.rr}; every query of a {B}-query batch on every shard",
+        "qps": steps * B / (ms / 1e3), "ms_per_step": ms / steps,
+        "e2e_qps": e2e_steps * B / (e2e_ms / 1e3),
+        "step_split_ms": {"search": t_search / steps, "all_gather": t_xchg / steps, "merge": t_merge / steps},
+        "all_gather_share": xchg_max / ms if ms > 0 else None,
+        "exchange_bytes_per_rank_per_step": M.per_rank(S, world) * M.block_words(B, k) * 4,
+        "recall_at_10": round(rec_mean, 4), "queries_scored": len(rec),
+        "merged_equal": bool(ok_all),
+        "merged_check": f"{n_check} queries: every rank's per-shard lists equal the oracle's search of that shard "
+                        f"(ids, distances, counts, visited); the GPU merge of the gathered lists equals the host "
+                        f"merge rule (distance, shard, rank)",
+        "shards_per_rank": len(mine), "build_or_load_s": round(build_s, 1),
+        "gpu_launches_per_step": len(mine) + 1,
+    }
+
+
 def run_sharded(args):
     """Collection split into `args.shards` contiguous per-shard graphs (shard s
     on rank s % world): every query is searched on every shard, the per-shard
@@ -385,23 +534,9 @@ def run_sharded(args):
     # exact kNN of the whole collection: exact per local shard, exchanged and merged
     truth = []
     for b in range(N_BATCHES):
-        gi = torch.zeros((len(mine), B, k), dtype=torch.int32, device="cuda")
-        gd = torch.zeros((len(mine), B, k), dtype=torch.float32, device="cuda")
-        for j, sh in enumerate(mine):
-            L.check(lib.raven_knn_exact_device(shards[sh]._h, d_q[b].data_ptr(), B, k, gi[j].data_ptr(),
-                                               gd[j].data_ptr(), stream.cuda_stream))
-        torch.cuda.synchronize()
-        with torch.cuda.stream(stream):
-            packed = M.pack_lists(gi, gd, torch.full((len(mine), B), k, dtype=torch.int32, device="cuda"))
-            if dist:
-                packed = M.exchange_shard_lists(packed, S)
-            ai, ad, ac = M.unpack_lists(packed, k)
-            oi = torch.zeros((B, k), dtype=torch.int32, device="cuda")
-            od = torch.zeros((B, k), dtype=torch.float32, device="cuda")
-        L.check(lib.raven_merge_topk_device(ai.data_ptr(), ad.data_ptr(), ac.data_ptr(), S, B, k, shard_n,
-                                            oi.data_ptr(), od.data_ptr(), None, stream.cuda_stream))
-        torch.cuda.synchronize()
-        truth.append(oi.cpu().numpy().view(np.uint32))
+        ti, _, _ = coll.exact(d_q[b], k, stream)
+        stream.synchronize()
+        truth.append(ti.cpu().numpy().view(np.uint32))
     for i in range(max(args.warmup, N_BATCHES)):
         coll.search(d_q[i % N_BATCHES], params, stream)
     torch.cuda.synchronize()
@@ -621,6 +756,11 @@ def main():
     e2e_s = max_over_ranks(e2e_ev[0].elapsed_time(e2e_ev[1]) / 1e3, device=torch.device("cuda", dev_id))
     e2e_value = e2e_steps * B * world / e2e_s
 
+    # the sharded-collection layout at this N (all ranks take part)
+    sharded = None
+    if not args.no_sharded:
+        sharded = sharded_record(args, base, world, rank, dev_id, steps=args.steps)
+
     sweep = None
     if (args.sweep or not args.no_extras) and rank == 0:
         sweep = {}
@@ -732,6 +872,7 @@ def main():
                                         "(the reference reaches 0.95 at ef=50 on SIFT-1M)",
             "ef50_point": ef50,
             "parity": parity,
+            "sharded": sharded,
             "recall_at_10": round(recall, 4), "queries_scored": int(got.shape[0]),
             "bad_status_queries": bad_status,
             "avg_visited": float(st["visited"].mean()), "avg_expansions": float(st["expansions"].mean()),

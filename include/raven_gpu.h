@@ -57,6 +57,8 @@ extern "C" {
 
 #define RAVEN_QUANT_SQ4 0 /* GraphSearcher::with_sq4 / search_sq4  src/graph/vamana.rs:1578,1772 */
 #define RAVEN_QUANT_SQ8 1 /* GraphSearcher::with_sq8 / search_sq8  src/graph/vamana.rs:1568,1752 */
+#define RAVEN_QUANT_F32 2 /* GraphSearcher::search: the f32 traversal (greedy_search_vec_reuse),
+                             results = the first k of the pool, no rerank  src/graph/vamana.rs:1627-1672 */
 
 typedef struct raven_graph raven_graph; /* VamanaGraph (host)            src/graph/vamana.rs:85 */
 typedef struct raven_index raven_index; /* searcher state on one GPU     src/graph/vamana.rs:1428 */
@@ -94,12 +96,13 @@ RAVEN_API int raven_graph_build(const float* vectors, uint64_t n, uint32_t dim, 
  * counterpart on a GPU; replaces the search + prune loop of VamanaGraph::build,
  * src/graph/vamana.rs:106-201). Same batches, random stream, connect step and
  * final prune as raven_graph_build; each batch's nodes are searched by the
- * engine's search kernel (entry = medoid, ef = l_build; the beam uses SQ4
- * distances, so visited sets can differ slightly from an f32 search) and their
- * visited sets pruned by DirectionalPrune on the GPU with f32 distances in the
- * AVX-512 summation order. DirectionalPrune only (cfg->directional = 1);
- * l_build <= 256, r_max <= 64, dim <= 256. The layered navigation is built on
- * the host as in raven_graph_build. */
+ * engine's search kernel in its f32 mode (greedy_search_vec_build,
+ * src/graph/vamana.rs:530-567: entry = medoid, ef = l_build, f32 distances in
+ * the AVX-512 summation order) and their visited sets pruned by
+ * DirectionalPrune on the GPU with the same distances, so the graph is the one
+ * raven_graph_build makes, byte for byte. DirectionalPrune only
+ * (cfg->directional = 1); l_build <= 256, r_max <= 64, dim <= 256. The layered
+ * navigation is built on the host as in raven_graph_build. */
 RAVEN_API int raven_graph_build_gpu(const float* vectors, uint64_t n, uint32_t dim, const raven_build_config* cfg,
                                     int device, raven_graph** out);
 /* Serializable::load + VamanaGraph::deserialize (src/memory/serialize.rs:146, src/graph/vamana.rs:1326). */
@@ -215,6 +218,18 @@ RAVEN_API int raven_knn_exact_device(raven_index* ix, const float* d_queries, ui
 RAVEN_API int raven_merge_topk_device(const uint32_t* d_ids, const float* d_dists, const uint32_t* d_counts,
                             uint32_t n_shards, uint64_t nq, uint32_t k, uint64_t shard_size, uint32_t* d_out_ids,
                             float* d_out_dists, uint32_t* d_out_counts, void* stream);
+
+/* The same merge read straight from the buffer an all-gather of per-rank
+ * blocks leaves behind (no reference counterpart). The buffer holds world x
+ * per_rank shard blocks, per_rank = ceil(n_shards / world); shard s (on rank
+ * s % world, its slot s / world there) is block (s % world) * per_rank +
+ * s / world. A block is nq*(2k+1) 32-bit words: ids u32 [nq][k], distances
+ * f32 [nq][k], counts u32 [nq] (a search's ids / dists / counts outputs laid
+ * end to end). Blocks past the last shard are ignored. Device buffers. */
+RAVEN_API int raven_merge_topk_gathered_device(const void* d_gathered, uint32_t n_shards, uint32_t world,
+                                               uint32_t per_rank, uint64_t nq, uint32_t k, uint64_t shard_size,
+                                               uint32_t* d_out_ids, float* d_out_dists, uint32_t* d_out_counts,
+                                               void* stream);
 
 typedef struct {
   uint32_t max_ef;      /* largest pool capacity (fixed ef or adaptive max) */

@@ -659,7 +659,7 @@ struct OracleParams {
   uint32_t ef;
   uint32_t k;
   uint32_t rerank_factor;
-  uint32_t quant;  // 0 = SQ4, 1 = SQ8
+  uint32_t quant;  // 0 = SQ4, 1 = SQ8, 2 = f32 traversal (GraphSearcher::search)
   uint32_t adaptive;
   float gamma;
   uint32_t min_ef, max_ef;
@@ -682,10 +682,18 @@ struct Worker {
   std::vector<uint8_t> code;
 };
 
+// GraphSearcher::search (the f32 traversal) — src/graph/vamana.rs:1627-1672:
+// the same entry and adaptive ef, greedy_search_vec_reuse (:588-666: the
+// loop above with l2_simd distances and one prefetched line per vector), then
+// the pool sorted by total_cmp and truncated to k (the pool is already in
+// ascending order; equal distances keep pool order, the tie rule used
+// throughout).
 int search_one(const Index& ix, const float* q, const OracleParams& p, Worker& w, QueryOut* out,
                bool want_history) {
   const size_t dim = ix.dim;
-  if (p.quant == 0) {
+  if (p.quant == 2) {
+    // no query code
+  } else if (p.quant == 0) {
     w.code.assign(ix.sq4_bytes, 0);
     sq4_encode(ix.sq4, q, w.code.data());
   } else {
@@ -714,7 +722,13 @@ int search_one(const Index& ix, const float* q, const OracleParams& p, Worker& w
   SearchStats st;
   std::vector<std::pair<uint32_t, float>> cands;
   const uint8_t* qc = w.code.data();
-  if (p.quant == 0) {
+  if (p.quant == 2) {
+    cands = greedy_search_q(
+        ix, entry, ef, w.visited, w.pool,
+        [&](uint32_t id) { return l2_avx512_order(q, ix.vectors.data() + (size_t)id * dim, dim); },
+        [&](uint32_t id) { return (const uint8_t*)(ix.vectors.data() + (size_t)id * dim); }, 1, p.prefetch_offset,
+        &st);
+  } else if (p.quant == 0) {
     const size_t cb = ix.sq4_bytes;
     cands = greedy_search_q(
         ix, entry, ef, w.visited, w.pool,
@@ -731,6 +745,11 @@ int search_one(const Index& ix, const float* q, const OracleParams& p, Worker& w
   out->n_nav = n_nav;
   out->expansions = st.expansions;
   if (want_history) out->history = w.visited.history;
+  if (p.quant == 2) {
+    if (cands.size() > p.k) cands.resize(p.k);
+    out->results = cands;
+    return 0;
+  }
   size_t rr = std::max<uint32_t>(p.rerank_factor, 1);  // with_rerank_factor clamps >= 1 (:1547-1550)
   out->results = rerank_f32(ix, q, cands, p.k, rr, p.rerank_f16 != 0);
   return 0;

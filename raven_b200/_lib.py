@@ -25,6 +25,7 @@ RAVEN_ELIMIT = -10
 
 RAVEN_QUANT_SQ4 = 0
 RAVEN_QUANT_SQ8 = 1
+RAVEN_QUANT_F32 = 2
 
 u32p = C.POINTER(C.c_uint32)
 f32p = C.POINTER(C.c_float)
@@ -134,6 +135,9 @@ SIGNATURES = {
                                          C.c_void_p]),
     "raven_merge_topk_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint64, C.c_uint32,
                                           C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "raven_merge_topk_gathered_device": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64,
+                                                   C.c_uint32, C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                   C.c_void_p]),
     "raven_limits": (None, [C.POINTER(Limits)]),
     "raven_index_set_tuning": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
     "raven_last_error": (C.c_char_p, []),

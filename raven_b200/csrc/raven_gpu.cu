@@ -406,32 +406,44 @@ __global__ void f16_convert_kernel(const float* __restrict__ in, uint64_t total,
 }
 
 // Shard merge: ids are shard-local; global id = shard * shard_size + local.
+// Shard s's lists start at block b(s) = (s % W) * P + s / W of each array:
+// ids at ids + b(s) * stride_i, distances at ds + b(s) * stride_d, counts at
+// counts + b(s) * stride_c, each [nq][k] (counts [nq]). W = 1, P = n_shards
+// is the shard-major layout; W ranks x P blocks is the layout an all-gather
+// of per-rank blocks (shard s on rank s % W, slot s / W) leaves behind.
+// One warp per query: each valid entry's output rank is the number of valid
+// entries before it in (distance, shard, rank) order.
+struct MergeLayout {
+  uint32_t W, P;
+  uint64_t stride_i, stride_d, stride_c;
+  __device__ uint64_t block(uint32_t s) const { return (uint64_t)(s % W) * P + s / W; }
+};
+
 __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ ds,
-                                   const uint32_t* __restrict__ counts, uint32_t n_shards, uint64_t nq, uint32_t k,
-                                   uint64_t shard_size, uint32_t* __restrict__ out_i, float* __restrict__ out_d,
-                                   uint32_t* __restrict__ out_c) {
+                                   const uint32_t* __restrict__ counts, MergeLayout L, uint32_t n_shards, uint64_t nq,
+                                   uint32_t k, uint64_t shard_size, uint32_t* __restrict__ out_i,
+                                   float* __restrict__ out_d, uint32_t* __restrict__ out_c) {
   const uint64_t qi = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (qi >= nq) return;
   const uint32_t total = n_shards * k;
+  auto cnt_of = [&](uint32_t sh) { return counts ? min(counts[L.block(sh) * L.stride_c + qi], k) : k; };
+  auto dist_at = [&](uint32_t sh, uint32_t r) { return ds[L.block(sh) * L.stride_d + qi * k + r]; };
   uint32_t valid_total = 0;
-  for (uint32_t sh = 0; sh < n_shards; ++sh) valid_total += counts ? min(counts[sh * nq + qi], k) : k;
+  for (uint32_t sh = 0; sh < n_shards; ++sh) valid_total += cnt_of(sh);
   for (uint32_t e = lane; e < total; e += 32) {
     const uint32_t sh = e / k, r = e % k;
-    const uint32_t cnt = counts ? min(counts[sh * nq + qi], k) : k;
-    if (r >= cnt) continue;
-    const size_t o = ((size_t)sh * nq + qi) * k + r;
-    const float d = ds[o];
+    if (r >= cnt_of(sh)) continue;
+    const float d = dist_at(sh, r);
     uint32_t rank = 0;
     for (uint32_t f = 0; f < total; ++f) {
       const uint32_t fs = f / k, fr = f % k;
-      const uint32_t fc = counts ? min(counts[fs * nq + qi], k) : k;
-      if (fr >= fc) continue;
-      const float df = ds[((size_t)fs * nq + qi) * k + fr];
+      if (fr >= cnt_of(fs)) continue;
+      const float df = dist_at(fs, fr);
       rank += (df < d) || (df == d && (fs < sh || (fs == sh && fr < r)));
     }
     if (rank < k) {
-      out_i[qi * k + rank] = (uint32_t)(sh * shard_size + ids[o]);
+      out_i[qi * k + rank] = (uint32_t)(sh * shard_size + ids[L.block(sh) * L.stride_i + qi * k + r]);
       out_d[qi * k + rank] = d;
     }
   }
@@ -475,6 +487,8 @@ cudaError_t dispatch_cpl(int cpl, bool occ, const SearchArgs& a, uint32_t smem, 
 }
 cudaError_t dispatch(int quant, int cpl, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
                      int* blocks) {
+  if (quant == RAVEN_QUANT_F32)
+    return occ ? occupancy_t<2, 1>(a.pool_cap, smem, blocks) : launch_t<2, 1>(a, smem, grid, st);
   return quant == 0 ? dispatch_cpl<0>(cpl, occ, a, smem, grid, st, blocks)
                     : dispatch_cpl<1>(cpl, occ, a, smem, grid, st, blocks);
 }
@@ -503,6 +517,7 @@ std::vector<uint32_t> ef_table(uint32_t S, uint32_t min_ef, uint32_t max_ef, flo
 
 struct Plan {
   int quant, cpl, hash_bits, spill_bits;
+  uint32_t f32_stage_rows;  // f32 traversal: neighbour rows staged per round
   uint32_t pool_cap;  // beam pool entries per warp: ef_cap rounded up to 32
   uint32_t ef_cap;
   uint32_t smem_warp, smem_block;
@@ -512,15 +527,18 @@ struct Plan {
 
 int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   if (!p) return fail(RAVEN_EINVAL, "null search params");
-  if (p->quant != RAVEN_QUANT_SQ4 && p->quant != RAVEN_QUANT_SQ8) return fail(RAVEN_EINVAL, "unknown quant");
-  if (!ix->has_q[p->quant])
+  if (p->quant != RAVEN_QUANT_SQ4 && p->quant != RAVEN_QUANT_SQ8 && p->quant != RAVEN_QUANT_F32)
+    return fail(RAVEN_EINVAL, "unknown quant");
+  if (p->quant != RAVEN_QUANT_F32 && !ix->has_q[p->quant])
     return fail(RAVEN_ESTATE, p->quant == 0 ? "search_sq4 requires with_sq4() first (index uploaded without SQ4)"
                                             : "search_sq8 requires with_sq8() first (index uploaded without SQ8)");
   if (p->k == 0) return fail(RAVEN_EINVAL, "k must be >= 1");
   if (p->rerank_f16 && !ix->d_vec16)
     return fail(RAVEN_ESTATE, "with_f16 requires an index uploaded with build_f16");
   pl->quant = p->quant;
-  pl->cpl = (int)(ix->q_stride[p->quant] / 16);
+  const bool f32 = p->quant == RAVEN_QUANT_F32;
+  pl->cpl = f32 ? 1 : (int)(ix->q_stride[p->quant] / 16);
+  pl->f32_stage_rows = f32 ? (ix->dim_pad <= 128 ? 16u : 8u) : 0u;
   uint32_t ef_cap;
   if (p->adaptive) {
     if (p->max_ef < p->min_ef) return fail(RAVEN_EINVAL, "max_ef must be >= min_ef");
@@ -564,9 +582,74 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   // the visited table doubles as the row staging area: it must hold a row
   while ((1u << hb) < ix->dim_pad) ++hb;
   pl->hash_bits = (int)hb;
-  pl->smem_warp = warp_smem_bytes(ix->dim_pad, ix->q_stride[p->quant], pl->pool_cap, hb, ix->r_pad);
+  pl->smem_warp = warp_smem_bytes(ix->dim_pad, f32 ? 0u : ix->q_stride[p->quant], pl->pool_cap, hb, ix->r_pad,
+                                  pl->f32_stage_rows);
   pl->smem_block = pl->smem_warp * kWarpsPerBlock;
   return RAVEN_OK;
+}
+
+// Kernel arguments shared by every search launch (the caller sets the
+// queries, the scratch areas and the work counter).
+void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params* p, const raven_search_outputs* o,
+               SearchArgs* out) {
+  SearchArgs& a = *out;
+  const bool f32 = pl.quant == RAVEN_QUANT_F32;
+  a.vec = ix->d_vec;
+  a.dim = ix->dim;
+  a.dim_pad = ix->dim_pad;
+  a.vec_c = ix->dim / 16;
+  a.vec_rem = ix->dim % 16;
+  a.adj = ix->d_adj;
+  a.r_pad = ix->r_pad;
+  a.vec16 = ix->d_vec16;
+  a.rerank_f16 = p->rerank_f16 ? 1 : 0;
+  a.pool_cap = pl.pool_cap;
+  a.codes = f32 ? nullptr : ix->d_codes[pl.quant];
+  a.code_stride = f32 ? 0u : ix->q_stride[pl.quant];
+  a.q_inv = f32 ? nullptr : ix->d_qparams[pl.quant] + 3 * ix->dim;
+  a.q_neg = f32 ? nullptr : ix->d_qparams[pl.quant] + 4 * ix->dim;
+  a.levels = pl.quant == 0 ? 15.0f : 255.0f;
+  a.dist_bits = 32;
+  if (!f32) {
+    // largest SQ distance: (levels^2) per dimension over the padded code
+    const uint64_t per_dim = pl.quant == 0 ? 225ull : 65025ull;
+    const uint64_t dims = pl.quant == 0 ? (uint64_t)ix->q_stride[0] * 2 : (uint64_t)ix->q_stride[1];
+    const uint64_t mx = per_dim * dims;
+    uint32_t b = 0;
+    while (b < 32 && (mx >> b) != 0) ++b;
+    a.dist_bits = b;
+  }
+  a.entry = ix->entry;
+  a.nav = ix->has_nav ? 1 : 0;
+  a.nav_entry_h = ix->nav_entry_h;
+  a.nav_max_level = ix->nav_max_level;
+  a.nav_k = ix->nav_k;
+  a.nav_stride_levels = ix->nav_stride_levels;
+  a.nav_vec = ix->d_nav_vec;
+  a.nav_e = ix->d_nav_e;
+  a.nav_gid = ix->d_nav_gid;
+  a.adaptive = p->adaptive ? 1 : 0;
+  a.samples = ix->d_samples;
+  a.n_samples = (uint32_t)ix->h_samples.size();
+  a.ef_mid = pl.ef_mid;
+  a.ef_fixed = p->ef;
+  a.k = p->k;
+  a.rr = std::max<uint32_t>(p->rerank_factor, 1);
+  a.hash_bits = pl.hash_bits;
+  a.spill_bits = pl.spill_bits;
+  a.smem_per_warp = pl.smem_warp;
+  a.f32_stage_rows = pl.f32_stage_rows;
+  a.ids = o->ids;
+  a.dists = o->dists;
+  a.counts = o->counts;
+  a.visited = o->visited;
+  a.ef_used = o->ef_used;
+  a.status = o->status;
+  a.n_nav = o->n_nav;
+  a.expansions = o->expansions;
+  a.history = o->history;
+  a.hist_cap = o->history ? o->history_cap : 0;
+  a.hist_len = o->history_len;
 }
 
 // Runs the search (or the nav-only descent) for device buffers.
@@ -575,7 +658,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   Plan pl;
   raven_search_params nav_p{};
   if (nav_only) {
-    nav_p.quant = ix->has_q[0] ? 0 : 1;
+    nav_p.quant = ix->has_q[0] ? RAVEN_QUANT_SQ4 : ix->has_q[1] ? RAVEN_QUANT_SQ8 : RAVEN_QUANT_F32;
     nav_p.ef = 1;
     nav_p.k = 1;
     p = &nav_p;
@@ -611,65 +694,13 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
     return fail(RAVEN_ECUDA, std::string("scratch setup: ") + cudaGetErrorString(e));
   }
   SearchArgs a{};
-  a.vec = ix->d_vec;
-  a.dim = ix->dim;
-  a.dim_pad = ix->dim_pad;
-  a.vec_c = ix->dim / 16;
-  a.vec_rem = ix->dim % 16;
-  a.adj = ix->d_adj;
-  a.r_pad = ix->r_pad;
-  a.vec16 = ix->d_vec16;
-  a.rerank_f16 = (!nav_only && p->rerank_f16) ? 1 : 0;
-  a.pool_cap = pl.pool_cap;
-  a.codes = ix->d_codes[pl.quant];
-  a.code_stride = ix->q_stride[pl.quant];
-  a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
-  a.q_neg = ix->d_qparams[pl.quant] + 4 * ix->dim;
-  a.levels = pl.quant == 0 ? 15.0f : 255.0f;
-  {
-    // largest SQ distance: (levels^2) per dimension over the padded code
-    const uint64_t per_dim = pl.quant == 0 ? 225ull : 65025ull;
-    const uint64_t dims = pl.quant == 0 ? (uint64_t)ix->q_stride[0] * 2 : (uint64_t)ix->q_stride[1];
-    const uint64_t mx = per_dim * dims;
-    uint32_t b = 0;
-    while (b < 32 && (mx >> b) != 0) ++b;
-    a.dist_bits = b;
-  }
-  a.entry = ix->entry;
-  a.nav = ix->has_nav ? 1 : 0;
-  a.nav_entry_h = ix->nav_entry_h;
-  a.nav_max_level = ix->nav_max_level;
-  a.nav_k = ix->nav_k;
-  a.nav_stride_levels = ix->nav_stride_levels;
-  a.nav_vec = ix->d_nav_vec;
-  a.nav_e = ix->d_nav_e;
-  a.nav_gid = ix->d_nav_gid;
-  a.adaptive = p->adaptive ? 1 : 0;
-  a.samples = ix->d_samples;
-  a.n_samples = (uint32_t)ix->h_samples.size();
+  fill_args(ix, pl, p, o, &a);
   a.ef_table = table;
-  a.ef_mid = pl.ef_mid;
-  a.ef_fixed = p->ef;
-  a.k = p->k;
-  a.rr = std::max<uint32_t>(p->rerank_factor, 1);
-  a.hash_bits = pl.hash_bits;
-  a.spill_bits = pl.spill_bits;
   a.spill = spill;
   a.n_slots = slots;
-  a.smem_per_warp = pl.smem_warp;
   a.queries = d_q;
   a.nq = nq;
-  a.ids = o->ids;
-  a.dists = o->dists;
-  a.counts = o->counts;
-  a.visited = o->visited;
-  a.ef_used = o->ef_used;
-  a.status = o->status;
-  a.n_nav = o->n_nav;
-  a.expansions = o->expansions;
-  a.history = o->history;
-  a.hist_cap = o->history ? o->history_cap : 0;
-  a.hist_len = o->history_len;
+  a.rerank_f16 = (!nav_only && p->rerank_f16) ? 1 : 0;
   a.counter = counter;
   a.nav_only = nav_only;
   e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
@@ -958,7 +989,6 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
   // AdaptiveEf samples: nav.initialize distances of base vectors 0..min(n,2000)
   if (o.build_adaptive) {
     if (!nav) return bail2(fail(RAVEN_ESTATE, "AdaptiveEf requires layered nav (enable_layered_nav=true)"));
-    if (!ix->has_q[0] && !ix->has_q[1]) return bail2(fail(RAVEN_ESTATE, "AdaptiveEf needs a quantiser"));
     uint32_t S = (uint32_t)std::min<uint64_t>(n, 2000);
     uint32_t* d_e = nullptr;
     float* d_d = nullptr;
@@ -1298,9 +1328,30 @@ int raven_merge_topk_device(const uint32_t* d_ids, const float* d_dists, const u
   if (n_shards == 0 || k == 0) return fail(RAVEN_EINVAL, "n_shards and k must be >= 1");
   if (nq == 0) return RAVEN_OK;
   cudaStream_t st = (cudaStream_t)stream;
-  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(d_ids, d_dists, d_counts, n_shards, nq, k,
-                                                                        shard_size, d_out_ids, d_out_dists,
+  const MergeLayout lay{1u, n_shards, nq * k, nq * k, nq};
+  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(d_ids, d_dists, d_counts, lay, n_shards, nq,
+                                                                        k, shard_size, d_out_ids, d_out_dists,
                                                                         d_out_counts);
+  CU(cudaGetLastError());
+  return RAVEN_OK;
+}
+
+int raven_merge_topk_gathered_device(const void* d_gathered, uint32_t n_shards, uint32_t world, uint32_t per_rank,
+                                     uint64_t nq, uint32_t k, uint64_t shard_size, uint32_t* d_out_ids,
+                                     float* d_out_dists, uint32_t* d_out_counts, void* stream) {
+  NvtxRange nvtx_range("raven.merge_topk_gathered");
+  if (!d_gathered || !d_out_ids || !d_out_dists) return fail(RAVEN_EINVAL, "null argument");
+  if (n_shards == 0 || k == 0 || world == 0) return fail(RAVEN_EINVAL, "n_shards, world and k must be >= 1");
+  if ((uint64_t)per_rank * world < n_shards || (uint64_t)(per_rank - 1) * world >= n_shards)
+    return fail(RAVEN_EINVAL, "per_rank must be ceil(n_shards / world)");
+  if (nq == 0) return RAVEN_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const uint64_t block = nq * (2ull * k + 1);  // words per shard block: ids, distances, counts
+  const uint32_t* base = (const uint32_t*)d_gathered;
+  const MergeLayout lay{world, per_rank, block, block, block};
+  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(
+      base, (const float*)(base + nq * k), base + 2 * nq * k, lay, n_shards, nq, k, shard_size, d_out_ids, d_out_dists,
+      d_out_counts);
   CU(cudaGetLastError());
   return RAVEN_OK;
 }
@@ -1429,64 +1480,13 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   if (!pl.table.empty())
     CU(cudaMemcpyAsync(table, pl.table.data(), pl.table.size() * 4, cudaMemcpyHostToDevice, st));
   SearchArgs a{};
-  a.vec = ix->d_vec;
-  a.dim = ix->dim;
-  a.dim_pad = ix->dim_pad;
-  a.vec_c = ix->dim / 16;
-  a.vec_rem = ix->dim % 16;
-  a.adj = ix->d_adj;
-  a.r_pad = ix->r_pad;
-  a.vec16 = ix->d_vec16;
-  a.rerank_f16 = p->rerank_f16 ? 1 : 0;
-  a.pool_cap = pl.pool_cap;
-  a.codes = ix->d_codes[pl.quant];
-  a.code_stride = ix->q_stride[pl.quant];
-  a.q_inv = ix->d_qparams[pl.quant] + 3 * ix->dim;
-  a.q_neg = ix->d_qparams[pl.quant] + 4 * ix->dim;
-  a.levels = pl.quant == 0 ? 15.0f : 255.0f;
-  {
-    const uint64_t per_dim = pl.quant == 0 ? 225ull : 65025ull;
-    const uint64_t dims = pl.quant == 0 ? (uint64_t)ix->q_stride[0] * 2 : (uint64_t)ix->q_stride[1];
-    const uint64_t mx = per_dim * dims;
-    uint32_t b = 0;
-    while (b < 32 && (mx >> b) != 0) ++b;
-    a.dist_bits = b;
-  }
-  a.entry = ix->entry;
-  a.nav = ix->has_nav ? 1 : 0;
-  a.nav_entry_h = ix->nav_entry_h;
-  a.nav_max_level = ix->nav_max_level;
-  a.nav_k = ix->nav_k;
-  a.nav_stride_levels = ix->nav_stride_levels;
-  a.nav_vec = ix->d_nav_vec;
-  a.nav_e = ix->d_nav_e;
-  a.nav_gid = ix->d_nav_gid;
-  a.adaptive = p->adaptive ? 1 : 0;
-  a.samples = ix->d_samples;
-  a.n_samples = (uint32_t)ix->h_samples.size();
+  fill_args(ix, pl, p, o, &a);
   a.ef_table = table;
-  a.ef_mid = pl.ef_mid;
-  a.ef_fixed = p->ef;
-  a.k = p->k;
-  a.rr = std::max<uint32_t>(p->rerank_factor, 1);
-  a.hash_bits = pl.hash_bits;
   a.spill_bits = sb;
   a.spill = spill;
   a.n_slots = slots;
-  a.smem_per_warp = pl.smem_warp;
   a.queries = d_q;
   a.nq = nq;
-  a.ids = o->ids;
-  a.dists = o->dists;
-  a.counts = o->counts;
-  a.visited = o->visited;
-  a.ef_used = o->ef_used;
-  a.status = o->status;
-  a.n_nav = o->n_nav;
-  a.expansions = o->expansions;
-  a.history = o->history;
-  a.hist_cap = o->history ? o->history_cap : 0;
-  a.hist_len = o->history_len;
   a.counter = counter;
   a.nav_only = 0;
   const cudaError_t e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
@@ -1499,10 +1499,11 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
 // ---------------------------------------------------------------------------
 // Vamana build on the GPU (no reference counterpart on a GPU: it replaces the
 // per-batch candidate step of VamanaGraph::build, src/graph/vamana.rs:106-201).
-// Per batch: the search kernel (entry = medoid, L = l_build, visited history
-// recorded) gives each node's candidate set, build_prune_kernel applies
-// DirectionalPrune to it; the host build keeps the batch order, the connect
-// step and the final prune, and sends back every changed row.
+// Per batch: the search kernel in its f32 mode (greedy_search_vec_build,
+// vamana.rs:530-567: entry = medoid, L = l_build, visited history recorded)
+// gives each node's candidate set, build_prune_kernel applies DirectionalPrune
+// to it; the host build keeps the batch order, the connect step and the final
+// prune, and sends back every changed row.
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -1702,7 +1703,7 @@ struct GpuBuild : raven::BuildAccelerator {
       while (d < r && main_block[v * r + d] != raven::kSentinel) ++d;
       gr.g.degrees[v] = d;
     }
-    raven_upload_options o{device, 1, 0, 0, 0};
+    raven_upload_options o{device, 0, 0, 0, 0};  // the f32 traversal needs no codes
     int rc = raven_index_upload(&gr, h_vec, n_, dim, &o, &ix);
     if (rc) {
       if (err) *err = raven_last_error();
@@ -1744,7 +1745,7 @@ struct GpuBuild : raven::BuildAccelerator {
     p.ef = cfg.l_build;
     p.k = 1;
     p.rerank_factor = 1;
-    p.quant = RAVEN_QUANT_SQ4;
+    p.quant = RAVEN_QUANT_F32;  // greedy_search_vec_build: the f32 beam
     raven_search_outputs o{};
     o.ids = d_ids;
     o.dists = d_dists;

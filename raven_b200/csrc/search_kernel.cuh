@@ -11,6 +11,11 @@
 //      ordering                                         src/memory/visited.rs:88-103)
 //   5. f32 rerank of min(k*rr, |pool|) survivors        (src/graph/refiner.rs:45-61)
 //
+// QUANT selects the beam's distance: 0 SQ4 codes, 1 SQ8 codes, 2 the f32
+// vectors themselves (GraphSearcher::search, src/graph/vamana.rs:1627-1672, and
+// the build's greedy_search_vec_build, :530-567). With f32 distances there is
+// no query code and no rerank: the result is the first k entries of the pool.
+//
 // LinearPool equivalence used by the batch merge: the pool always holds the
 // first `ef` of all inserted candidates ordered by (distance, insertion order)
 // and the cursor is the first unexpanded entry. A new candidate therefore loses
@@ -93,6 +98,7 @@ struct SearchArgs {
   uint32_t* hist_len;
   unsigned long long* counter;
   int nav_only;  // 1: only run the descent; write entry to ids[q], distance to dists[q]
+  uint32_t f32_stage_rows;  // QUANT 2: rows staged per round for the beam's f32 distances
 };
 
 // Per-warp shared-memory carve-up (every piece 16-byte aligned).
@@ -106,14 +112,15 @@ struct WarpSmem {
   float* nd;          // 32
   uint32_t* rowbuf;   // 2 x r_pad: adjacency rows prefetched by cp.async
   uint32_t* ht;       // 1 << hash_bits; also the row staging area outside the beam search
+  float* fstage;      // QUANT 2: f32_stage_rows rows of the beam's new neighbours
 };
 
 __host__ __device__ inline uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
 __host__ __device__ inline uint32_t warp_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pool_cap,
-                                                    uint32_t hash_bits, uint32_t r_pad) {
+                                                    uint32_t hash_bits, uint32_t r_pad, uint32_t f32_stage_rows = 0) {
   return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(pool_cap * 4) + 3 * 128 + 2 * r_pad * 4 +
-         align16((1u << hash_bits) * 4);
+         align16((1u << hash_bits) * 4) + f32_stage_rows * dim_pad * 4;
 }
 
 __device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, uint32_t pool_cap) {
@@ -136,6 +143,8 @@ __device__ inline WarpSmem carve(uint8_t* base, const SearchArgs& a, uint32_t po
   s.rowbuf = (uint32_t*)(base + o);
   o += 2 * a.r_pad * 4;
   s.ht = (uint32_t*)(base + o);
+  o += align16((1u << a.hash_bits) * 4);
+  s.fstage = (float*)(base + o);
   return s;
 }
 
@@ -628,6 +637,12 @@ struct QChunk<0> {  // SQ4: sum (q-x)^2 = sum q^2 + sum x (x - 2q), nibbles unpa
 };
 
 template <>
+struct QChunk<2> {  // f32 beam: no code (distances come from the vectors)
+  __device__ inline void load(const uint8_t*, int) {}
+  __device__ inline int dist(uint4) const { return 0; }
+};
+
+template <>
 struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
   uint32_t q[4];
   __device__ inline void load(const uint8_t* qcode, int chunk) {
@@ -755,7 +770,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
     int sz = 0;
     if (status != 3) {
       // encode the query (natural dims read through the lane-major map)
-      if (QUANT == 0) {
+      if (QUANT == 2) {
+        // f32 beam: no query code
+      } else if (QUANT == 0) {
         for (uint32_t b = lane; b < a.code_stride; b += 32) {
           const uint32_t d0 = 2 * b, d1 = 2 * b + 1;
           const uint32_t lo =
@@ -783,7 +800,17 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       tcount = 1;
       if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
       vcount = 1;
-      {
+      if (QUANT == 2) {
+        // l2_simd(query, vectors[entry]) (src/graph/vamana.rs:603-606); non-negative
+        // f32 distances order like their bit patterns, which the pool compares
+        if (lane == 0) s.cand_id[0] = entry;
+        __syncwarp();
+        rows_dist(s.qf, s.fstage, a.f32_stage_rows, s.cand_id, 1, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd, lane);
+        if (lane == 0) {
+          s.pool_d[0] = __float_as_uint(s.nd[0]);
+          s.pool_id[0] = entry;
+        }
+      } else {
         int pd = 0;
         if (grp == 0) {
           const uint4 v = __ldg((const uint4*)(a.codes + (size_t)entry * a.code_stride) + sub);
@@ -847,7 +874,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
           // (a neighbour that turns out visited costs one wasted 16 B load per lane)
           uint4 data[CPL];
 #pragma unroll
-          for (int r = 0; r < CPL; ++r) {
+          for (int r = 0; r < (QUANT == 2 ? 0 : CPL); ++r) {
             const int idx = r * CPR + grp;
             const uint32_t cid_raw = __shfl_sync(kFull, id, idx & 31);
             const uint32_t cid = idx < deg ? cid_raw : 0u;  // address always in range
@@ -916,19 +943,31 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
             if (pos < a.hist_cap) a.history[qi * a.hist_cap + pos] = id;
           }
           vcount += nn;
-          // integer distances of the row (candidate idx -> cand_d[idx])
+          uint32_t my_d;
+          if (QUANT == 2) {
+            // f32 distances of the new neighbours only, in adjacency order
+            // (compacted), their rows staged in shared memory
+            const int cpos = __popc(newm & lanemask_lt(lane));
+            if (is_new) s.cand_id[cpos] = id;
+            __syncwarp();
+            rows_dist(s.qf, s.fstage, a.f32_stage_rows, s.cand_id, nn, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd,
+                      lane);
+            my_d = is_new ? __float_as_uint(s.nd[cpos]) : 0xffffffffu;
+          } else {
+            // integer distances of the row (candidate idx -> cand_d[idx])
 #pragma unroll
-          for (int r = 0; r < CPL; ++r) {
-            if (r * CPR < deg) {
-              int pdist = qc.dist(data[r]);
+            for (int r = 0; r < CPL; ++r) {
+              if (r * CPR < deg) {
+                int pdist = qc.dist(data[r]);
 #pragma unroll
-              for (int o = 1; o < CPL; o <<= 1) pdist += __shfl_xor_sync(kFull, pdist, o);
-              const int idx = r * CPR + grp;
-              if (sub == 0 && idx < deg) s.cand_d[idx] = (uint32_t)pdist;
+                for (int o = 1; o < CPL; o <<= 1) pdist += __shfl_xor_sync(kFull, pdist, o);
+                const int idx = r * CPR + grp;
+                if (sub == 0 && idx < deg) s.cand_d[idx] = (uint32_t)pdist;
+              }
             }
+            __syncwarp();
+            my_d = is_new ? s.cand_d[lane] : 0xffffffffu;
           }
-          __syncwarp();
-          const uint32_t my_d = is_new ? s.cand_d[lane] : 0xffffffffu;
           // merge the new neighbours (adjacency order) into the pool:
           // LinearPool::insert semantics, batched
           const bool full = sz == (int)ef;
@@ -1026,12 +1065,14 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       }
     }
 
-    // 5. rerank: exact f32 L2 of the first min(k*rr, sz) pool entries
-    const uint64_t krr = (uint64_t)a.k * (uint64_t)max(a.rr, 1u);
+    // 5. rerank: exact f32 L2 of the first min(k*rr, sz) pool entries. With
+    // the f32 beam the pool already holds those distances (the same values):
+    // the result is its first min(k, sz) entries (search(), vamana.rs:1667-1671)
+    const uint64_t krr = QUANT == 2 ? (uint64_t)a.k : (uint64_t)a.k * (uint64_t)max(a.rr, 1u);
     const uint64_t krr_k = krr > (uint64_t)a.k ? krr : (uint64_t)a.k;
     const int rn = (int)(krr_k < (uint64_t)sz ? krr_k : (uint64_t)sz);
     float* rdist = (float*)s.pool_d;  // pool distances are no longer needed
-    for (int c0 = 0; c0 < rn; c0 += 32) {
+    for (int c0 = 0; c0 < (QUANT == 2 ? 0 : rn); c0 += 32) {
       const int cn = min(32, rn - c0);
       if (lane < cn) s.cand_id[lane] = s.pool_id[c0 + lane] & ~kChecked;
       __syncwarp();

@@ -3,8 +3,9 @@
 * `Graph`          — VamanaGraph (src/graph/vamana.rs:85): build / load / save.
 * `GraphSearcher`  — the Rust query builder (src/graph/vamana.rs:1428-2110):
                      new / with_sq4 / with_sq8 / with_rerank_factor /
-                     with_prefetch_offset / with_adaptive_ef / search_sq4 /
-                     search_sq8 / batch_search / last_visited_count / last_ef_used.
+                     with_prefetch_offset / with_adaptive_ef / search (f32) /
+                     search_sq4 / search_sq8 / batch_search / last_visited_count /
+                     last_ef_used.
 * `Index`, `Searcher` — the PyO3 module `raven` (src/python.rs:27-361) with the
                      same signatures, defaults, errors and result layout.
 
@@ -323,10 +324,20 @@ class GraphSearcher:
         return p
 
     def _search(self, queries, k: int, quant: int):
-        if not self._want["sq4" if quant == L.RAVEN_QUANT_SQ4 else "sq8"]:
+        if quant != L.RAVEN_QUANT_F32 and not self._want["sq4" if quant == L.RAVEN_QUANT_SQ4 else "sq8"]:
             name = "sq4" if quant == L.RAVEN_QUANT_SQ4 else "sq8"
             raise RuntimeError(f"search_{name} requires with_{name}() first")
         return self._device_index().search(queries, self._params(k, quant))
+
+    def search(self, query, k: int) -> List[Tuple[int, float]]:
+        """GraphSearcher::search (src/graph/vamana.rs:1627-1672): the beam over
+        f32 distances (greedy_search_vec_reuse), no rerank; the first k of the
+        pool."""
+        r = self._search(np.asarray(query, dtype=np.float32)[None, :], k, L.RAVEN_QUANT_F32)
+        self._last_visited = int(r["visited"][0])
+        self._last_ef = int(r["ef_used"][0])
+        c = int(r["counts"][0])
+        return [(int(i), float(d)) for i, d in zip(r["ids"][0, :c], r["dists"][0, :c])]
 
     def search_sq4(self, query, k: int) -> List[Tuple[int, float]]:
         r = self._search(np.asarray(query, dtype=np.float32)[None, :], k, L.RAVEN_QUANT_SQ4)
@@ -343,8 +354,9 @@ class GraphSearcher:
         return [(int(i), float(d)) for i, d in zip(r["ids"][0, :c], r["dists"][0, :c])]
 
     def batch_search(self, queries, k: int) -> List[List[Tuple[int, float]]]:
-        """Branch order SQ8 > SQ4 (vamana.rs:2063-2091); f32 traversal is not offered."""
-        quant = L.RAVEN_QUANT_SQ8 if self._want["sq8"] else L.RAVEN_QUANT_SQ4
+        """Branch order SQ8 > SQ4 > f32 traversal (vamana.rs:2063-2091)."""
+        quant = (L.RAVEN_QUANT_SQ8 if self._want["sq8"] else
+                 L.RAVEN_QUANT_SQ4 if self._want["sq4"] else L.RAVEN_QUANT_F32)
         q = _f32c(queries)
         r = self._search(q, k, quant)
         return [[(int(i), float(d)) for i, d in zip(r["ids"][j, : r["counts"][j]], r["dists"][j, : r["counts"][j]])]

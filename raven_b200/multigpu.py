@@ -14,15 +14,16 @@ or multi-GPU layer. Two layouts map that onto several B200s:
   Shard s lives on rank s % world. Every rank searches every query on each of
   its shards; the per-shard top-k lists (f32 distance, shard-local id, count)
   are exchanged by one all-gather and merged per query on the GPU by
-  `raven_merge_topk_device`, ties ordered by (distance, shard, rank in the
+  `raven_merge_topk_gathered_device`, ties ordered by (distance, shard, rank in the
   shard's list). Searching each shard exactly as the reference searches one
   graph and merging by that rule gives the same ids as running the reference
   on every shard and merging its outputs on the host.
 
-The exchange packs a shard's lists into one int32 tensor [nq, 2k + 1]
-(ids, distance bit patterns, count) so that a step needs one all-gather;
-it works unchanged on NCCL (CUDA tensors) and gloo (CPU tensors, used by the
-CPU tests of this module).
+The search kernel writes each shard's lists (ids, distances, counts) into one
+block of the rank's send buffer, one all-gather moves every rank's blocks, and
+the merge kernel reads the gathered buffer where it lies (shard s is block
+(s % world) * per_rank + s // world). The exchange works on NCCL (CUDA
+tensors) and gloo (CPU tensors, used by the CPU tests of this module).
 """
 from __future__ import annotations
 
@@ -62,38 +63,61 @@ def max_over_ranks(x: float, device: Optional[torch.device] = None, group=None) 
     return float(t.item())
 
 
-def pack_lists(ids: torch.Tensor, dists: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
-    """[n, nq, k] ids (int32 view of u32), [n, nq, k] f32, [n, nq] counts ->
-    [n, nq, 2k + 1] int32 (distances as bit patterns)."""
-    if ids.shape != dists.shape or counts.shape != ids.shape[:2]:
-        raise ValueError("ids, dists must be [n, nq, k] and counts [n, nq]")
-    return torch.cat([ids.to(torch.int32), dists.contiguous().view(torch.int32),
-                      counts.to(torch.int32).unsqueeze(-1)], dim=-1)
+def block_words(nq: int, k: int) -> int:
+    """32-bit words of one shard's lists in the exchange layout: ids u32
+    [nq][k], distances f32 [nq][k], counts u32 [nq], end to end."""
+    return nq * (2 * k + 1)
 
 
-def unpack_lists(packed: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    ids = packed[..., :k].contiguous()
-    dists = packed[..., k:2 * k].contiguous().view(torch.float32)
-    counts = packed[..., 2 * k].contiguous()
-    return ids, dists, counts
+def per_rank(n_shards: int, world: int) -> int:
+    """Shard blocks every rank sends (ranks holding fewer pad with unused blocks)."""
+    return -(-n_shards // world)
 
 
-def exchange_shard_lists(local: torch.Tensor, n_shards: int, group=None) -> torch.Tensor:
-    """All-gather the packed lists of this rank's shards ([len(shards_of_rank),
-    nq, 2k + 1]) and return every shard's lists in shard order
-    ([n_shards, nq, 2k + 1]). Ranks holding fewer shards pad their block, so
-    every rank sends the same shape."""
+def gathered_block(shard: int, world: int, per: int) -> int:
+    """Block index of `shard` in the all-gathered buffer: rank shard % world,
+    slot shard // world there."""
+    return (shard % world) * per + shard // world
+
+
+def block_views(buf: torch.Tensor, j: int, nq: int, k: int):
+    """(ids, dists, counts) views of block j of a flat int32 buffer: ids
+    [nq, k] int32 (u32 bit patterns), dists [nq, k] f32, counts [nq] int32."""
+    w = block_words(nq, k)
+    b = buf[j * w:(j + 1) * w]
+    return (b[:nq * k].view(nq, k), b[nq * k:2 * nq * k].view(torch.float32).view(nq, k), b[2 * nq * k:])
+
+
+def exchange_blocks(send: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather every rank's send buffer (its shard blocks) into one flat
+    buffer, rank-major. NCCL on CUDA tensors; gloo (CPU tests) gathers a list."""
     world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    mine = shards_of_rank(n_shards, world, rank)
-    if local.shape[0] != len(mine):
-        raise ValueError(f"rank {rank} holds {len(mine)} shards, got lists for {local.shape[0]}")
-    per = -(-n_shards // world)
-    block = local.new_zeros((per,) + tuple(local.shape[1:]))
-    block[:local.shape[0]] = local
-    gathered = [torch.empty_like(block) for _ in range(world)]
-    dist.all_gather(gathered, block, group=group)
-    return torch.stack([gathered[s % world][s // world] for s in range(n_shards)])
+    recv = send.new_empty(world * send.numel())
+    if send.is_cuda:
+        dist.all_gather_into_tensor(recv, send, group=group)
+    else:
+        parts = list(recv.chunk(world))
+        dist.all_gather(parts, send, group=group)
+    return recv
+
+
+def read_gathered(recv: torch.Tensor, n_shards: int, world: int, nq: int, k: int):
+    """Host-side view of a gathered buffer in shard order: ids [S, nq, k]
+    (uint32), dists [S, nq, k], counts [S, nq] as numpy arrays."""
+    import numpy as np
+
+    per = per_rank(n_shards, world)
+    a = recv.cpu().numpy()
+    w = block_words(nq, k)
+    ids = np.zeros((n_shards, nq, k), np.uint32)
+    ds = np.zeros((n_shards, nq, k), np.float32)
+    cs = np.zeros((n_shards, nq), np.uint32)
+    for s in range(n_shards):
+        b = a[gathered_block(s, world, per) * w:][:w]
+        ids[s] = b[:nq * k].view(np.uint32).reshape(nq, k)
+        ds[s] = b[nq * k:2 * nq * k].view(np.float32).reshape(nq, k)
+        cs[s] = b[2 * nq * k:].view(np.uint32)
+    return ids, ds, cs
 
 
 class ShardedCollection:
@@ -102,6 +126,13 @@ class ShardedCollection:
     `shards` maps shard number -> DeviceIndex for the shards this rank holds
     (exactly `shards_of_rank(n_shards, world, rank)`); every shard but the last
     covers `shard_size` global ids.
+
+    A step writes each local shard's top-k lists straight into this rank's
+    send buffer (one block per shard, the layout of `block_views`), gathers
+    every rank's buffer with one all-gather, and merges the gathered blocks
+    in place with raven_merge_topk_gathered_device: no packing or reordering
+    copies. The buffers are kept per (nq, k) and reused, so the tensors a step
+    returns are valid until the next step with the same shape.
     """
 
     def __init__(self, shards: Dict[int, "object"], n_shards: int, shard_size: int, group=None):
@@ -116,32 +147,66 @@ class ShardedCollection:
         self.shard_size = shard_size
         self.group = group
         self.world = world
+        self.per = per_rank(n_shards, world)
+        self._bufs = {}
 
-    def search(self, d_queries: torch.Tensor, params: L.SearchParams, stream: torch.cuda.Stream):
+    def _buffers(self, nq: int, k: int, dev, stream):
+        key = (nq, k, str(dev))
+        if key not in self._bufs:
+            with torch.cuda.stream(stream):
+                send = torch.zeros(self.per * block_words(nq, k), dtype=torch.int32, device=dev)
+                recv = torch.zeros(self.world * send.numel(), dtype=torch.int32, device=dev) if self.world > 1 else send
+                out = (torch.zeros((nq, k), dtype=torch.int32, device=dev),
+                       torch.zeros((nq, k), dtype=torch.float32, device=dev),
+                       torch.zeros(nq, dtype=torch.int32, device=dev))
+            self._bufs[key] = (send, recv, out)
+        return self._bufs[key]
+
+    def _exchange_merge(self, send, recv, out, nq: int, k: int, stream, marks=None):
+        lib = L.load()
+        if self.world > 1:
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(recv, send, group=self.group)
+        if marks is not None:
+            marks[1].record(stream)
+        L.check(lib.raven_merge_topk_gathered_device(recv.data_ptr(), self.n_shards, self.world, self.per, nq, k,
+                                                     self.shard_size, out[0].data_ptr(), out[1].data_ptr(),
+                                                     out[2].data_ptr(), stream.cuda_stream))
+        return out
+
+    def search(self, d_queries: torch.Tensor, params: L.SearchParams, stream: torch.cuda.Stream, marks=None):
         """Every query on every shard, then exchange and merge. Returns device
         tensors (ids [nq, k] int32 view of global u32 ids, dists [nq, k],
-        counts [nq]); queued on `stream`."""
+        counts [nq]); queued on `stream`. `marks`: two CUDA events recorded
+        after the searches and after the exchange (for the step's breakdown)."""
         lib = L.load()
         nq, k = d_queries.shape[0], params.k
-        dev = d_queries.device
-        with torch.cuda.stream(stream):  # every allocation and fill is ordered on the launch stream
-            ids = torch.zeros((len(self.order), nq, k), dtype=torch.int32, device=dev)
-            ds = torch.zeros((len(self.order), nq, k), dtype=torch.float32, device=dev)
-            cnt = torch.zeros((len(self.order), nq), dtype=torch.int32, device=dev)
+        send, recv, out = self._buffers(nq, k, d_queries.device, stream)
         for j, s in enumerate(self.order):
-            out = L.SearchOutputs(ids=C.cast(ids[j].data_ptr(), L.u32p), dists=C.cast(ds[j].data_ptr(), L.f32p),
-                                  counts=C.cast(cnt[j].data_ptr(), L.u32p))
+            ids, ds, cnt = block_views(send, j, nq, k)
+            o = L.SearchOutputs(ids=C.cast(ids.data_ptr(), L.u32p), dists=C.cast(ds.data_ptr(), L.f32p),
+                                counts=C.cast(cnt.data_ptr(), L.u32p))
             L.check(lib.raven_search_batch_device(self.shards[s]._h, d_queries.data_ptr(), nq, C.byref(params),
-                                                  C.byref(out), stream.cuda_stream))
-        with torch.cuda.stream(stream):
-            packed = pack_lists(ids, ds, cnt)
-            if self.world > 1:
-                packed = exchange_shard_lists(packed, self.n_shards, self.group)
-            all_i, all_d, all_c = unpack_lists(packed, k)
-            out_i = torch.zeros((nq, k), dtype=torch.int32, device=dev)
-            out_d = torch.zeros((nq, k), dtype=torch.float32, device=dev)
-            out_c = torch.zeros(nq, dtype=torch.int32, device=dev)
-        L.check(lib.raven_merge_topk_device(all_i.data_ptr(), all_d.data_ptr(), all_c.data_ptr(), self.n_shards, nq, k,
-                                            self.shard_size, out_i.data_ptr(), out_d.data_ptr(), out_c.data_ptr(),
-                                            stream.cuda_stream))
-        return out_i, out_d, out_c
+                                                  C.byref(o), stream.cuda_stream))
+        if marks is not None:
+            marks[0].record(stream)
+        return self._exchange_merge(send, recv, out, nq, k, stream, marks)
+
+    def gathered(self, nq: int, k: int, device) -> torch.Tensor:
+        """The gathered buffer of the last step with this shape (every shard's
+        lists, block (s % world) * per + s // world)."""
+        return self._bufs[(nq, k, str(device))][1]
+
+    def exact(self, d_queries: torch.Tensor, k: int, stream: torch.cuda.Stream):
+        """The exact top-k of the whole collection: the exact kNN of every local
+        shard (raven_knn_exact_device), exchanged and merged the same way."""
+        lib = L.load()
+        nq = d_queries.shape[0]
+        send, recv, out = self._buffers(nq, k, d_queries.device, stream)
+        for j, s in enumerate(self.order):
+            ids, ds, cnt = block_views(send, j, nq, k)
+            L.check(lib.raven_knn_exact_device(self.shards[s]._h, d_queries.data_ptr(), nq, k, ids.data_ptr(),
+                                               ds.data_ptr(), stream.cuda_stream))
+            with torch.cuda.stream(stream):
+                cnt.fill_(k)
+        return self._exchange_merge(send, recv, out, nq, k, stream)

@@ -1,8 +1,10 @@
 """Vamana build with the per-batch search + DirectionalPrune on the GPU
 (raven_graph_build_gpu): a valid graph (degrees within r_max, no self loops,
 no repeated neighbours, ids in range, navigation built), deterministic (two
-builds serialise to the same bytes), searchable with oracle parity, and of
-the same quality as the host build (recall@10 at ef=50 within 0.02).
+builds serialise to the same bytes), and the same graph as the host build
+(raven_graph_build), byte for byte, on integer and on float data: the GPU's
+candidate search is the f32 beam of greedy_search_vec_build and its prune
+takes the same decisions with the same distances.
 """
 import os
 import tempfile
@@ -50,31 +52,31 @@ def test_gpu_build_structure_and_determinism(data):
     assert _bytes(g1) == _bytes(_build(base, 0))
 
 
-def test_gpu_build_search_parity_and_quality(data, oracle):
+def test_gpu_build_equals_host_build(data, oracle):
     from raven_b200 import _lib as L
-    from raven_b200.index import DeviceIndex
+    from raven_b200 import datasets
+    from raven_b200.index import DeviceIndex, Graph
 
     base, q = data
-    gi, _ = oracle.bruteforce(base, q, 10)
-    recalls = {}
-    for name, dev_id in (("gpu", 0), ("host", None)):
-        g = _build(base, dev_id)
-        dev = DeviceIndex(g, base, sq4=True)
-        p = L.SearchParams(ef=50, k=10, rerank_factor=8, prefetch_offset=8, quant=0, adaptive=0, gamma=0.0, min_ef=0,
-                           max_ef=0)
-        got = dev.search(q, p)
-        assert np.all(got["status"] == 0)
-        recalls[name] = np.mean([len(set(got["ids"][i]) & set(gi[i])) / 10 for i in range(q.shape[0])])
-        if name == "gpu":
-            with tempfile.TemporaryDirectory() as d:
-                path = os.path.join(d, "g.annx")
-                g.save(path)
-                oi = oracle.OracleIndex(path)
-            oi.set_vectors(base, sq4=True)
-            exp = oi.search(q, k=10, ef=50, rerank_factor=8)
-            np.testing.assert_array_equal(got["ids"], exp["ids"])
-            np.testing.assert_array_equal(got["visited"], exp["visited"])
-    assert recalls["gpu"] >= recalls["host"] - 0.02, recalls
+    gpu = _build(base, 0)
+    assert _bytes(gpu) == _bytes(_build(base, None))
+    # float data: the AVX-512 summation order decides both builds' comparisons
+    fb = datasets.clustered_unit(8000, 96, 80, 0.3, seed=21, centre_seed=22)
+    kw = dict(r=32, l=100, alpha=1.2, nav_m=16, directional=True, seed=9)
+    assert _bytes(Graph.build(fb, device=0, **kw)) == _bytes(Graph.build(fb, **kw))
+    # and the graph searches with oracle parity
+    dev = DeviceIndex(gpu, base, sq4=True)
+    p = L.SearchParams(ef=50, k=10, rerank_factor=8, prefetch_offset=8, quant=0, adaptive=0, gamma=0.0, min_ef=0,
+                       max_ef=0)
+    got = dev.search(q, p)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "g.annx")
+        gpu.save(path)
+        oi = oracle.OracleIndex(path)
+    oi.set_vectors(base, sq4=True)
+    exp = oi.search(q, k=10, ef=50, rerank_factor=8)
+    np.testing.assert_array_equal(got["ids"], exp["ids"])
+    np.testing.assert_array_equal(got["visited"], exp["visited"])
 
 
 def test_saved_index_serves_without_vectors(tmp_path, raven_lib):

@@ -86,6 +86,18 @@ def test_search_sq4_parity(small, ef, k, rr):
     _compare(got, exp)
 
 
+@pytest.mark.parametrize("ef,k", [(50, 10), (10, 10), (1, 1), (200, 10), (64, 32)])
+def test_search_f32_parity(small, ef, k):
+    """GraphSearcher::search: the beam over f32 distances, results = the first
+    k of the pool (no rerank)."""
+    from raven_b200 import _lib as L
+
+    base, q, g, dev, oi = small
+    got = dev.search(q, _params(ef=ef, k=k, quant=L.RAVEN_QUANT_F32), history_cap=4096)
+    exp = oi.search(q, k=k, ef=ef, quant=2, history_cap=4096)
+    _compare(got, exp)
+
+
 @pytest.mark.parametrize("ef", [40, 50, 100])
 def test_search_sq8_parity(small, ef):
     base, q, g, dev, oi = small
@@ -123,7 +135,7 @@ def test_float_data_parity_dim96(oracle, raven_lib):
     dev = DeviceIndex(g, base, sq4=True, sq8=True, adaptive=True)
     oi = _oracle_for(oracle, g, base)
     np.testing.assert_array_equal(dev.adaptive_samples(), oi.adaptive_samples())
-    for quant in (0, 1):
+    for quant in (0, 1, 2):
         got = dev.search(q, _params(ef=50, quant=quant), history_cap=4096)
         exp = oi.search(q, k=10, ef=50, rerank_factor=8, quant=quant, history_cap=4096)
         _compare(got, exp, exact_dists=True)
@@ -155,7 +167,7 @@ def test_degree_padding_and_wide_rows(oracle, raven_lib, r_max):
         deg = int(rng.integers(0, r_max + 1))
         rows.append([int(x) for x in rng.choice(n, size=deg, replace=False)])
     base, q, dev, oi = _handmade(oracle, n, dim, r_max, rows)
-    for quant in (0, 1):
+    for quant in (0, 1, 2):
         got = dev.search(q, _params(ef=40, quant=quant), history_cap=2048)
         exp = oi.search(q, k=10, ef=40, rerank_factor=8, quant=quant, history_cap=2048)
         _compare(got, exp)

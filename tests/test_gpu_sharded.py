@@ -1,6 +1,7 @@
 """Sharded collection on the GPU: every query searched on every shard's own
-graph, per-shard top-k lists exchanged (all-gather) and merged by
-raven_merge_topk_device. Checked against the oracle's search of each shard,
+graph, per-shard top-k lists written into per-rank send blocks, exchanged
+(all-gather) and merged in place by raven_merge_topk_gathered_device. Checked
+against the oracle's search of each shard,
 merged on the host by the (distance, shard, rank) rule: ids, distances and
 counts bit-exact.
 
@@ -114,3 +115,46 @@ def test_sharded_two_gpus_nccl(shard_data):
         np.testing.assert_array_equal(got["c"], wc)
         np.testing.assert_array_equal(got["i"], wi)
         np.testing.assert_array_equal(got["d"], wd)
+
+
+def test_gathered_merge_layout_three_ranks(shard_data, oracle):
+    """raven_merge_topk_gathered_device on the buffer three ranks' all-gather
+    would leave (4 shards, two blocks per rank, the last block unused), built
+    on one GPU from the oracle's per-shard lists: equal to the host merge."""
+
+    import torch
+
+    from raven_b200 import _lib as L
+    from raven_b200 import multigpu as M
+
+    d, base, q, (wi, wd, wc) = shard_data
+    ids = np.zeros((N_SHARDS, NQ, K), np.uint32)
+    ds = np.zeros((N_SHARDS, NQ, K), np.float32)
+    cs = np.zeros((N_SHARDS, NQ), np.uint32)
+    for s in range(N_SHARDS):
+        oi = oracle.OracleIndex(os.path.join(d, f"shard{s}.annx"))
+        oi.set_vectors(np.ascontiguousarray(base[s * SHARD_SIZE:(s + 1) * SHARD_SIZE]), sq4=True)
+        r = oi.search(q, k=K, ef=50, rerank_factor=8)
+        ids[s], ds[s], cs[s] = r["ids"], r["dists"], r["counts"]
+    world = 3
+    per = M.per_rank(N_SHARDS, world)
+    buf = torch.full((world * per * M.block_words(NQ, K),), -1, dtype=torch.int32)
+    for s in range(N_SHARDS):
+        bi, bd, bc = M.block_views(buf, M.gathered_block(s, world, per), NQ, K)
+        bi.copy_(torch.from_numpy(ids[s].view(np.int32)))
+        bd.copy_(torch.from_numpy(ds[s]))
+        bc.copy_(torch.from_numpy(cs[s].view(np.int32)))
+    g = buf.cuda()
+    oi_ = torch.zeros((NQ, K), dtype=torch.int32, device="cuda")
+    od = torch.zeros((NQ, K), dtype=torch.float32, device="cuda")
+    oc = torch.zeros(NQ, dtype=torch.int32, device="cuda")
+    lib = L.load()
+    L.check(lib.raven_merge_topk_gathered_device(g.data_ptr(), N_SHARDS, world, per, NQ, K, SHARD_SIZE,
+                                                 oi_.data_ptr(), od.data_ptr(), oc.data_ptr(), None))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(oi_.cpu().numpy().view(np.uint32), wi)
+    np.testing.assert_array_equal(od.cpu().numpy(), wd)
+    np.testing.assert_array_equal(oc.cpu().numpy().view(np.uint32), wc)
+    with pytest.raises(L.RavenError):  # per_rank must be ceil(n_shards / world)
+        L.check(lib.raven_merge_topk_gathered_device(g.data_ptr(), N_SHARDS, world, per + 1, NQ, K, SHARD_SIZE,
+                                                     oi_.data_ptr(), od.data_ptr(), oc.data_ptr(), None))

@@ -1,5 +1,5 @@
 """Host logic of the multi-GPU layouts (raven_b200/multigpu.py), run on CPU:
-query partition, shard placement, the packed list format, and — with two gloo
+query partition, shard placement, the exchange block layout, and — with two gloo
 ranks — the max-over-ranks timing reduction and the all-gather that brings
 every shard's top-k lists to every rank, followed by the (distance, shard,
 rank) merge, checked against a single-process merge of the same lists.
@@ -38,18 +38,29 @@ def test_shards_of_rank():
         assert got == list(range(8))
 
 
-def test_pack_roundtrip_keeps_bit_patterns():
+def test_block_layout_keeps_bit_patterns():
+    """A shard's lists written into a block of the exchange buffer and read
+    back in shard order through the gathered-buffer indexing (here three
+    ranks' buffers laid end to end, as an all-gather leaves them)."""
     rng = np.random.default_rng(3)
-    ids = torch.from_numpy(rng.integers(0, 2**32, size=(3, 5, 10), dtype=np.uint64).astype(np.uint32).view(np.int32))
-    d = rng.standard_normal((3, 5, 10)).astype(np.float32)
+    S, world, nq, k = 5, 3, 4, 10
+    ids = rng.integers(0, 2**32, size=(S, nq, k), dtype=np.uint64).astype(np.uint32)
+    d = rng.standard_normal((S, nq, k)).astype(np.float32)
     d[0, 0, :3] = [-0.0, np.inf, 1e-45]
-    ds = torch.from_numpy(d)
-    cnt = torch.from_numpy(rng.integers(0, 11, size=(3, 5)).astype(np.int32))
-    p = M.pack_lists(ids, ds, cnt)
-    assert p.dtype == torch.int32 and p.shape == (3, 5, 21)
-    i2, d2, c2 = M.unpack_lists(p, 10)
-    assert torch.equal(i2, ids) and torch.equal(c2, cnt)
-    assert np.array_equal(d2.numpy().view(np.uint32), d.view(np.uint32))
+    c = rng.integers(0, 11, size=(S, nq)).astype(np.uint32)
+    per = M.per_rank(S, world)
+    bufs = []
+    for r in range(world):
+        send = torch.zeros(per * M.block_words(nq, k), dtype=torch.int32)
+        for j, s in enumerate(M.shards_of_rank(S, world, r)):
+            bi, bd, bc = M.block_views(send, j, nq, k)
+            bi.copy_(torch.from_numpy(ids[s].view(np.int32)))
+            bd.copy_(torch.from_numpy(d[s]))
+            bc.copy_(torch.from_numpy(c[s].view(np.int32)))
+        bufs.append(send)
+    i2, d2, c2 = M.read_gathered(torch.cat(bufs), S, world, nq, k)
+    assert np.array_equal(i2, ids) and np.array_equal(c2, c)
+    assert np.array_equal(d2.view(np.uint32), d.view(np.uint32))
 
 
 def _free_port() -> int:
@@ -68,14 +79,18 @@ def _rank_main(rank, world, port, tmp, n_shards, k):
     try:
         # max-over-ranks timing reduction
         tmax = M.max_over_ranks(10.0 + rank)
-        # this rank's shards, packed, exchanged, merged
+        # this rank's shards written into its send blocks, exchanged, merged
         lists = np.load(os.path.join(tmp, "lists.npz"))
         mine = M.shards_of_rank(n_shards, world, rank)
-        packed = M.pack_lists(torch.from_numpy(lists["ids"][mine].view(np.int32)), torch.from_numpy(lists["d"][mine]),
-                              torch.from_numpy(lists["c"][mine].view(np.int32)))
-        full = M.exchange_shard_lists(packed, n_shards)
-        i, d, c = M.unpack_lists(full, k)
-        mi, md, mc = O.merge_shard_lists(i.numpy().view(np.uint32), d.numpy(), c.numpy(), int(lists["size"]), k)
+        nq = lists["ids"].shape[1]
+        send = torch.zeros(M.per_rank(n_shards, world) * M.block_words(nq, k), dtype=torch.int32)
+        for j, s in enumerate(mine):
+            bi, bd, bc = M.block_views(send, j, nq, k)
+            bi.copy_(torch.from_numpy(lists["ids"][s].view(np.int32)))
+            bd.copy_(torch.from_numpy(lists["d"][s]))
+            bc.copy_(torch.from_numpy(lists["c"][s].view(np.int32)))
+        i, d, c = M.read_gathered(M.exchange_blocks(send), n_shards, world, nq, k)
+        mi, md, mc = O.merge_shard_lists(i, d, c, int(lists["size"]), k)
         np.savez(os.path.join(tmp, f"rank{rank}.npz"), tmax=tmax, i=mi, d=md, c=mc,
                  slice=np.array(M.query_slice(1001, world, rank)))
     finally:
