@@ -826,23 +826,31 @@ def main():
         lat_q, lat_n = 64, 300
         ql = d_q[0][:lat_q]
         lat = {}
-        for name, pl in (("ef%d" % args.ef, params),
-                         ("adaptive gamma=2.4 (35,75)", L.SearchParams(ef=75, k=k, rerank_factor=args.rr,
-                                                                        prefetch_offset=8, quant=quant, adaptive=1,
-                                                                        gamma=2.4, min_ef=35, max_ef=75))):
+        ad24 = L.SearchParams(ef=75, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=1,
+                              gamma=2.4, min_ef=35, max_ef=75)
+        # small batches run one CTA per query (the default up to one query per
+        # SM); the persistent one-warp-per-query kernel is timed beside it
+        runs = (("ef%d" % args.ef, params, lat_q, None), ("adaptive gamma=2.4 (35,75)", ad24, lat_q, None),
+                ("ef%d, 1 query" % args.ef, params, 1, None),
+                ("ef%d, persistent kernel" % args.ef, params, lat_q, 0))
+        for name, pl, nql, sb in runs:
+            if sb is not None:
+                dev.set_small_batch(sb)
             ol = outs(0, with_stats=False)
             for _ in range(20):
-                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), lat_q, C.byref(pl), C.byref(ol),
+                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), nql, C.byref(pl), C.byref(ol),
                                                       stream.cuda_stream))
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(lat_n)]
             for a_, b_ in evs:
                 a_.record(stream)
-                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), lat_q, C.byref(pl), C.byref(ol),
+                L.check(lib.raven_search_batch_device(dev._h, ql.data_ptr(), nql, C.byref(pl), C.byref(ol),
                                                       stream.cuda_stream))
                 b_.record(stream)
             torch.cuda.synchronize()
+            if sb is not None:
+                dev.set_small_batch(torch.cuda.get_device_properties(dev_id).multi_processor_count)
             ts = sorted(a_.elapsed_time(b_) * 1e3 for a_, b_ in evs)
-            lat[name] = {"p50_us": round(ts[len(ts) // 2], 1), "p99_us": round(ts[int(len(ts) * 0.99)], 1)}
+            lat[name] = {"queries": nql, "p50_us": round(ts[len(ts) // 2], 1), "p99_us": round(ts[int(len(ts) * 0.99)], 1)}
         latency = {"queries_per_launch": lat_q, "launches": lat_n, "device_time_per_launch": lat}
 
     parity = None

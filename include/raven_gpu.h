@@ -244,6 +244,15 @@ RAVEN_API void raven_limits(raven_limits_t* out);
  * global spill-table slots per resident warp (10..20, 0 = keep). */
 RAVEN_API int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bits);
 
+/* Small-batch path (no reference counterpart): a search of at most `max_nq`
+ * queries runs one CTA of four warps per query, with the visited set in a
+ * 2^15-slot shared-memory table, instead of the persistent one-warp-per-query
+ * kernel; results are identical. Default after upload: the device's SM count.
+ * 0 disables it (every batch uses the persistent kernel). Applies to SQ4/SQ8
+ * searches without rerank_f16 through raven_search_batch and
+ * raven_search_batch_device. */
+RAVEN_API int raven_index_set_small_batch(raven_index* ix, uint64_t max_nq);
+
 RAVEN_API const char* raven_last_error(void);
 RAVEN_API const char* raven_version(void);
 

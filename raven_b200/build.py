@@ -18,7 +18,7 @@ LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libraven_gpu.so")
 
 SOURCES = ["raven_gpu.cu", "host_index.cpp"]
-DEPS = SOURCES + ["search_kernel.cuh", "knn_tc.cuh", "host_index.h"]
+DEPS = SOURCES + ["search_kernel.cuh", "search_cta.cuh", "knn_tc.cuh", "host_index.h"]
 
 
 def nvcc_path() -> str:

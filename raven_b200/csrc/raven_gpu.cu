@@ -26,6 +26,7 @@
 #include "../../include/raven_gpu.h"
 #include "host_index.h"
 #include "knn_tc.cuh"
+#include "search_cta.cuh"
 #include "search_kernel.cuh"
 
 using namespace raven_dev;
@@ -58,6 +59,7 @@ struct raven_index {
   // launch tuning
   int hash_bits_override = 0;
   int spill_bits_override = 0;
+  uint64_t small_batch_max = 0;  // batches of at most this many queries run one CTA per query
 };
 
 namespace {
@@ -493,6 +495,25 @@ cudaError_t dispatch(int quant, int cpl, bool occ, const SearchArgs& a, uint32_t
                     : dispatch_cpl<1>(cpl, occ, a, smem, grid, st, blocks);
 }
 
+template <int QUANT, int CPL>
+cudaError_t launch_cta_t(const SearchArgs& a, uint32_t smem, uint64_t nq, cudaStream_t st) {
+  auto k = search_cta_kernel<QUANT, CPL>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  k<<<(unsigned)nq, kCtaThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+template <int QUANT>
+cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, uint32_t smem, uint64_t nq, cudaStream_t st) {
+  switch (cpl) {
+    case 1: return launch_cta_t<QUANT, 1>(a, smem, nq, st);
+    case 2: return launch_cta_t<QUANT, 2>(a, smem, nq, st);
+    case 4: return launch_cta_t<QUANT, 4>(a, smem, nq, st);
+    case 8: return launch_cta_t<QUANT, 8>(a, smem, nq, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 constexpr uint32_t kMaxEf = 256;
 constexpr uint32_t kMaxDimSq4 = 256;
 constexpr uint32_t kMaxDimSq8 = 128;
@@ -652,6 +673,45 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
   a.hist_len = o->history_len;
 }
 
+// Small batches: one CTA of four warps per query (search_cta.cuh), the visited
+// set in a 2^15-slot shared table; per-query global spill tables (2^13-slot
+// level A, level B 8x) stay allocated for exactness, touched only by a query
+// that fills the shared table. Same results as the batch kernel.
+int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p, const Plan& pl,
+                   const raven_search_outputs* o, cudaStream_t st) {
+  // the tuning hook can shrink the table (tests reach the spill levels this way)
+  uint32_t hb = ix->hash_bits_override ? std::min<uint32_t>((uint32_t)ix->hash_bits_override, kCtaHashBits)
+                                       : kCtaHashBits;
+  while ((1u << hb) < ix->dim_pad) ++hb;
+  const uint32_t kSpill = ix->spill_bits_override ? std::min<uint32_t>((uint32_t)ix->spill_bits_override, 13u) : 13u;
+  const uint32_t smem = cta_smem_bytes(ix->dim_pad, ix->q_stride[pl.quant], pl.pool_cap, hb, ix->r_pad);
+  const size_t spill_bytes = (size_t)nq * (9ull << kSpill) * 4;
+  const size_t table_bytes = pl.table.size() * 4;
+  uint8_t* scratch = nullptr;
+  CU(cudaMallocAsync((void**)&scratch, spill_bytes + ((table_bytes + 255) & ~(size_t)255) + 256, st));
+  uint32_t* spill = (uint32_t*)scratch;
+  uint32_t* table = (uint32_t*)(scratch + spill_bytes);
+  cudaError_t e = cudaSuccess;
+  if (table_bytes) e = cudaMemcpyAsync(table, pl.table.data(), table_bytes, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) {
+    SearchArgs a{};
+    fill_args(ix, pl, p, o, &a);
+    a.hash_bits = hb;
+    a.spill_bits = kSpill;
+    a.ef_table = table;
+    a.spill = spill;
+    a.n_slots = nq;
+    a.queries = d_q;
+    a.nq = nq;
+    a.counter = nullptr;
+    a.nav_only = 0;
+    e = pl.quant == 0 ? dispatch_cta_cpl<0>(pl.cpl, a, smem, nq, st) : dispatch_cta_cpl<1>(pl.cpl, a, smem, nq, st);
+  }
+  cudaFreeAsync(scratch, st);
+  if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("small-batch search launch: ") + cudaGetErrorString(e));
+  return RAVEN_OK;
+}
+
 // Runs the search (or the nav-only descent) for device buffers.
 int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
                const raven_search_outputs* o, cudaStream_t st, int nav_only) {
@@ -668,6 +728,8 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   if (nq == 0) return RAVEN_OK;
   if (!o || !o->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
   CU(cudaSetDevice(ix->device));
+  if (!nav_only && nq <= ix->small_batch_max && pl.quant != RAVEN_QUANT_F32 && !p->rerank_f16)
+    return run_search_cta(ix, d_q, nq, p, pl, o, st);
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
@@ -881,6 +943,7 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
   if (cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, o.device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(RAVEN_ECUDA, "device query / stream creation failed"));
+  ix->small_batch_max = (uint64_t)ix->num_sms;  // one query per SM
   {
     // per-call scratch comes from the device's stream-ordered pool; keep freed
     // blocks cached instead of returning them to the driver at every sync
@@ -1353,6 +1416,12 @@ int raven_merge_topk_gathered_device(const void* d_gathered, uint32_t n_shards, 
       base, (const float*)(base + nq * k), base + 2 * nq * k, lay, n_shards, nq, k, shard_size, d_out_ids, d_out_dists,
       d_out_counts);
   CU(cudaGetLastError());
+  return RAVEN_OK;
+}
+
+int raven_index_set_small_batch(raven_index* ix, uint64_t max_nq) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  ix->small_batch_max = max_nq;
   return RAVEN_OK;
 }
 

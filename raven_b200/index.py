@@ -199,6 +199,10 @@ class DeviceIndex:
     def set_tuning(self, hash_bits: int = 0, spill_bits: int = 0) -> None:
         L.check(L.load().raven_index_set_tuning(self._h, hash_bits, spill_bits))
 
+    def set_small_batch(self, max_nq: int) -> None:
+        """Batches of at most `max_nq` queries run one CTA per query (0: never)."""
+        L.check(L.load().raven_index_set_small_batch(self._h, max_nq))
+
     def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True) -> dict:
         """Host-buffer batch search (raven_search_batch). Returns a dict of arrays."""
         q = _f32c(queries)
