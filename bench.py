@@ -74,7 +74,7 @@ def parse():
                     help="split the workload into this many per-shard graphs (all-gather + merge across ranks)")
     ap.add_argument("--shard-n", type=int, default=0, help="vectors per shard (default: workload n / shards)")
     ap.add_argument("--build-device", type=int, default=None,
-                    help="build a missing index with the GPU candidate step on this device (default: host build)")
+                    help="build a missing index with the GPU build on this device (default: this rank's GPU)")
     return ap.parse_args()
 
 
@@ -150,13 +150,23 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def load_workload(args, rank):
+def load_workload(args, rank, barrier=None, device=None):
+    """Base vectors, this rank's query batches and the cached graph. A missing
+    graph is built once (rank 0; the others wait at `barrier`) and saved; the
+    GPU build (`device`) gives the host build's graph byte for byte, faster."""
     from raven_b200 import datasets
 
     base, _ = datasets.make(args.workload, nq=1)
     qs = [datasets.make_queries(args.workload, args.batch, offset=rank * N_BATCHES + b) for b in range(N_BATCHES)]
     t0 = time.time()
-    g = datasets.load_or_build(args.workload, base=base, device=args.build_device)
+    dev = args.build_device if args.build_device is not None else device
+    if barrier is not None and rank != 0:
+        barrier()
+    # the other ranks wait, so the build's host part may use every core (torchrun
+    # sets OMP_NUM_THREADS=1)
+    g = datasets.load_or_build(args.workload, base=base, device=dev, threads=os.cpu_count() or 1)
+    if barrier is not None and rank == 0:
+        barrier()
     args.load_s = time.time() - t0
     return base, np.stack(qs), g
 
@@ -643,7 +653,7 @@ def main():
         torch.cuda.set_device(0)
     dev_id = torch.cuda.current_device()
 
-    base, qbatches, g = load_workload(args, rank)
+    base, qbatches, g = load_workload(args, rank, barrier=tdist.barrier if dist else None, device=dev_id)
     quant = L.RAVEN_QUANT_SQ4 if args.quant == "sq4" else L.RAVEN_QUANT_SQ8
     dev = DeviceIndex(g, base, device=dev_id, sq4=quant == 0, sq8=quant == 1, adaptive=True)
     if args.hash_bits or args.spill_bits:
@@ -888,7 +898,7 @@ def main():
             "l2": f"not flushed: index working set ~{(base.nbytes + base.shape[0] * (code_bytes + 4 * R)) / 2**20:.0f} "
                   f"MiB > 126 MB L2; {nb} distinct query batches rotate per step",
             "parallelism": f"replicated index, query-batch partition x{world}",
-            "index": f"{'GPU-built' if args.build_device is not None else 'host-built or cached'} graph, "
+            "index": f"cached graph or a GPU build (the host build's graph, byte for byte), "
                      f"loaded/built in {args.load_s:.1f} s",
             "wall_s_timed": wall,
         },

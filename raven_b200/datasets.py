@@ -141,7 +141,7 @@ def index_path(name: str, n: int | None = None) -> str:
 def load_or_build(name: str, base=None, n: int | None = None, threads: int = 0, verbose: bool = False,
                   device: int | None = None):
     """Load the cached graph for a workload or build and save it (on the host,
-    or with the GPU candidate step when `device` is given)."""
+    or with the GPU build on `device`, which makes the same graph)."""
     from .index import Graph
 
     path = index_path(name, n)
@@ -152,7 +152,7 @@ def load_or_build(name: str, base=None, n: int | None = None, threads: int = 0, 
     g = Graph.build(base, r=32, l=200, alpha=1.2, nav_m=32, directional=True, threads=threads, verbose=verbose,
                     device=device)
     _os.makedirs(DATA_DIR, exist_ok=True)
-    tmp = path + ".tmp"
+    tmp = f"{path}.tmp{_os.getpid()}"
     g.save(tmp)
     _os.replace(tmp, path)
     return g
