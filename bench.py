@@ -94,8 +94,12 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(name="search_sq4_gmm1m"):
-    """DRAM bytes per launch from the committed ncu summary (or None)."""
+def profiled_traffic(workload):
+    """DRAM bytes per launch of the search kernel on this workload, from the
+    committed ncu summary named for it (None when there is none)."""
+    name = {"gmm1m-d128-sparse": "search_sq4_gmm1m"}.get(workload)
+    if name is None:
+        return None
     for fn in sorted(os.listdir(os.path.join(ROOT, "profiles"))) if os.path.isdir(os.path.join(ROOT, "profiles")) else []:
         if fn.startswith(name) and fn.endswith(".md"):
             m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(os.path.join(ROOT, "profiles", fn)).read())
@@ -903,7 +907,7 @@ def main():
             "wall_s_timed": wall,
         },
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "frac": achieved / peak, "traffic": profiled_traffic(args.workload),
                      "peak_source": peak_kind,
                      "algorithmic_bytes_per_query": bytes_per_batch / B},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * dim * 4,
