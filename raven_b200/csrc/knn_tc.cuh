@@ -42,8 +42,6 @@ constexpr int kThreads = 32 * (4 + kEpiWarps);
 constexpr uint32_t kBlockBytes = kBN * kBK * 4;  // one operand block: 16 KB
 constexpr uint32_t kTmemCols = 2 * kBN;
 constexpr long long kWaitCycles = 1ll << 32;     // ~2 s: a longer wait is a fault
-constexpr int kQ = 8;                            // candidates an epilogue thread queues before inserting
-constexpr int kEpiThreads = 32 * kEpiWarps;
 
 template <int PASSES>
 struct Layout {
@@ -55,9 +53,7 @@ struct Layout {
   // barriers: a_full, full[S], empty[S], acc_full[2], acc_empty[2], drain; then the tmem slot
   static constexpr uint32_t kNumBars = 1 + 2 * kStages + 5;
   static constexpr uint32_t kTmemSlot = kBars + kNumBars * 8;
-  // per epilogue thread kQ queued (distance, id) pairs, entry i of thread t at i * kEpiThreads + t
-  static constexpr uint32_t kQueue = kTmemSlot + 16;
-  static constexpr uint32_t kBytes = kQueue + (uint32_t)kQ * kEpiThreads * 8 + 1024;  // + alignment slack
+  static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;  // + alignment slack
 };
 
 struct Params {
@@ -142,49 +138,16 @@ __device__ inline void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
-// Sorted insertion of (cd, ci) into this thread's top-k list (ascending by
-// (distance, id)); thr = the k-th distance held. One compact site per call,
-// no dynamic register indexing.
-template <int KT>
-__device__ __forceinline__ void list_insert(float cd, uint32_t ci, uint32_t k, float (&kd)[KT], uint32_t (&ki)[KT],
-                                   float& thr) {
-  if (!(cd < thr)) return;  // ids rise along the scan: an equal distance never displaces an entry held
-#pragma unroll
-  for (int m = 0; m < KT; ++m) {
-    const bool sw = cd < kd[m] || (cd == kd[m] && ci < ki[m]);
-    const float td = kd[m];
-    const uint32_t ti = ki[m];
-    kd[m] = sw ? cd : td;
-    ki[m] = sw ? ci : ti;
-    cd = sw ? td : cd;
-    ci = sw ? ti : ci;
-  }
-#pragma unroll
-  for (int m = 0; m < KT; ++m) thr = (uint32_t)m == k - 1 ? kd[m] : thr;
-}
-
-// Inserts this thread's queued candidates, in the order they were queued (the
-// scan order), the warp's lanes in step: as many rounds as the longest queue.
-template <int KT>
-__device__ __forceinline__ void flush_queue(const float* qd, const uint32_t* qid, int& qn, uint32_t k, float (&kd)[KT],
-                                   uint32_t (&ki)[KT], float& thr) {
-  const int rounds = (int)__reduce_max_sync(0xffffffffu, (unsigned)qn);
-  for (int i = 0; i < rounds; ++i)
-    if (i < qn) list_insert<KT>(qd[i * kEpiThreads], qid[i * kEpiThreads], k, kd, ki, thr);
-  qn = 0;
-}
-
 // 32 dot products of one query against base rows id0..id0+31: distances
-// |q|^2 + |x|^2 - 2 q.x; those below the current k-th distance are queued
-// (up to kQ per thread, in shared memory) and inserted into the sorted list
-// when some lane of the warp would overflow its queue, so that the warp's
-// lanes insert together instead of one lane at a time. A lane with more than
-// kQ candidates left after a flush inserts them directly. The common case
-// (nothing qualifies anywhere in the warp) costs an FMA and a min per element.
+// |q|^2 + |x|^2 - 2 q.x, and any that beat the current k-th distance go into
+// the sorted list. The common case (nothing qualifies) costs an FMA and a
+// min per element; insertions use one compact site, the candidate's value
+// picked by a select chain (no dynamic register indexing). Ids rise along the
+// scan, so an equal distance never displaces an entry already held and the
+// strict test keeps ties ordered by id.
 template <int KT>
-__device__ __forceinline__ void scan_chunk(const uint32_t (&v)[32], const float* xn, float qnorm, uint32_t id0, uint32_t k,
-                                  float (&kd)[KT], uint32_t (&ki)[KT], float& thr, float* qd, uint32_t* qid,
-                                  int& qn) {
+__device__ inline void scan_chunk(const uint32_t (&v)[32], const float* xn, float qnorm, uint32_t id0, uint32_t k,
+                                  float (&kd)[KT], uint32_t (&ki)[KT], float& thr) {
   const float4* xp = (const float4*)xn;
   float dv[32];
   float dmin = __int_as_float(0x7f800000);
@@ -197,33 +160,30 @@ __device__ __forceinline__ void scan_chunk(const uint32_t (&v)[32], const float*
     dv[4 * j + 3] = fmaf(-2.0f, __uint_as_float(v[4 * j + 3]), qnorm + f.w);
     dmin = fminf(dmin, fminf(fminf(dv[4 * j], dv[4 * j + 1]), fminf(dv[4 * j + 2], dv[4 * j + 3])));
   }
-  if (!__any_sync(0xffffffffu, dmin < thr)) return;
+  if (!(dmin < thr)) return;
   uint32_t cand = 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) cand |= (uint32_t)(dv[j] < thr) << j;
-  int nc = __popc(cand);
-  if (__any_sync(0xffffffffu, qn + nc > kQ)) {
-    flush_queue<KT>(qd, qid, qn, k, kd, ki, thr);
-    uint32_t still = 0;  // the flush may have lowered the bar
-#pragma unroll
-    for (int j = 0; j < 32; ++j) still |= (uint32_t)(dv[j] < thr) << j;
-    cand &= still;
-    nc = __popc(cand);
-  }
-  const bool direct = nc > kQ;
   while (cand) {
     const int j = __ffs(cand) - 1;
     cand &= cand - 1;
     float cd = 0.0f;
 #pragma unroll
     for (int m = 0; m < 32; ++m) cd = m == j ? dv[m] : cd;
-    if (direct) {
-      list_insert<KT>(cd, id0 + (uint32_t)j, k, kd, ki, thr);
-    } else {
-      qd[qn * kEpiThreads] = cd;
-      qid[qn * kEpiThreads] = id0 + (uint32_t)j;
-      ++qn;
+    if (!(cd < thr)) continue;  // an earlier insertion of this chunk raised the bar
+    uint32_t ci = id0 + (uint32_t)j;
+#pragma unroll
+    for (int m = 0; m < KT; ++m) {
+      const bool sw = cd < kd[m] || (cd == kd[m] && ci < ki[m]);
+      const float td = kd[m];
+      const uint32_t ti = ki[m];
+      kd[m] = sw ? cd : td;
+      ki[m] = sw ? ci : ti;
+      cd = sw ? td : cd;
+      ci = sw ? ti : ci;
     }
+#pragma unroll
+    for (int m = 0; m < KT; ++m) thr = (uint32_t)m == k - 1 ? kd[m] : thr;
   }
 }
 
@@ -374,9 +334,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       ki[j] = 0xffffffffu;
     }
     float thr = __int_as_float(0x7f800000);  // distance of the k-th entry held
-    float* qd = (float*)(smem + L::kQueue) + (warp - 4) * 32 + lane;  // this thread's queue
-    uint32_t* qid = (uint32_t*)(smem + L::kQueue) + kQ * kEpiThreads + (warp - 4) * 32 + lane;
-    int qn = 0;
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     constexpr int kHalf = kBN / 2;
     for (uint32_t t = 0; t < ntiles; ++t) {
@@ -403,16 +360,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             "=r"(vb[22]), "=r"(vb[23]), "=r"(vb[24]), "=r"(vb[25]), "=r"(vb[26]), "=r"(vb[27]), "=r"(vb[28]),
             "=r"(vb[29]), "=r"(vb[30]), "=r"(vb[31])
           : "r"(tmem + lane_base + (uint32_t)(b * kBN + half * kHalf + 32)));
-      scan_chunk<KT>(va, p.xn + row0 + half * kHalf, qnorm, (uint32_t)(row0 + half * kHalf), p.k, kd, ki, thr, qd,
-                     qid, qn);
+      scan_chunk<KT>(va, p.xn + row0 + half * kHalf, qnorm, (uint32_t)(row0 + half * kHalf), p.k, kd, ki, thr);
       asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-      scan_chunk<KT>(vb, p.xn + row0 + half * kHalf + 32, qnorm, (uint32_t)(row0 + half * kHalf + 32), p.k, kd, ki,
-                     thr, qd, qid, qn);
+      scan_chunk<KT>(vb, p.xn + row0 + half * kHalf + 32, qnorm, (uint32_t)(row0 + half * kHalf + 32), p.k, kd, ki, thr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(b));
     }
-    flush_queue<KT>(qd, qid, qn, p.k, kd, ki, thr);
     if (qi < p.nq) {
       const size_t o = (((size_t)sp * 2 + (size_t)half) * p.nq + qi) * p.k;
 #pragma unroll
