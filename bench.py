@@ -842,8 +842,8 @@ def main():
         lat = {}
         ad24 = L.SearchParams(ef=75, k=k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=1,
                               gamma=2.4, min_ef=35, max_ef=75)
-        # small batches run one CTA per query (the default up to one query per
-        # SM); the persistent one-warp-per-query kernel is timed beside it
+        # small batches run one CTA per query (by default up to one wave of
+        # CTAs); the persistent one-warp-per-query kernel is timed beside it
         runs = (("ef%d" % args.ef, params, lat_q, None), ("adaptive gamma=2.4 (35,75)", ad24, lat_q, None),
                 ("ef%d, 1 query" % args.ef, params, 1, None),
                 ("ef%d, persistent kernel" % args.ef, params, lat_q, 0))
@@ -862,7 +862,9 @@ def main():
                 b_.record(stream)
             torch.cuda.synchronize()
             if sb is not None:
-                dev.set_small_batch(torch.cuda.get_device_properties(dev_id).multi_processor_count)
+                from raven_b200.index import SMALL_BATCH_AUTO
+
+                dev.set_small_batch(SMALL_BATCH_AUTO)
             ts = sorted(a_.elapsed_time(b_) * 1e3 for a_, b_ in evs)
             lat[name] = {"queries": nql, "p50_us": round(ts[len(ts) // 2], 1), "p99_us": round(ts[int(len(ts) * 0.99)], 1)}
         latency = {"queries_per_launch": lat_q, "launches": lat_n, "device_time_per_launch": lat}

@@ -246,11 +246,13 @@ RAVEN_API int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t
 
 /* Small-batch path (no reference counterpart): a search of at most `max_nq`
  * queries runs one CTA of four warps per query, with the visited set in a
- * 2^15-slot shared-memory table, instead of the persistent one-warp-per-query
- * kernel; results are identical. Default after upload: the device's SM count.
- * 0 disables it (every batch uses the persistent kernel). Applies to SQ4/SQ8
- * searches without rerank_f16 through raven_search_batch and
+ * 2^14-slot shared-memory table, instead of the persistent one-warp-per-query
+ * kernel; results are identical. RAVEN_SMALL_BATCH_AUTO (the default after
+ * upload): as many queries as one wave of such CTAs holds (three per SM at dim
+ * 128); 0 disables it (every batch uses the persistent kernel). Applies to
+ * SQ4/SQ8 searches without rerank_f16 through raven_search_batch and
  * raven_search_batch_device. */
+#define RAVEN_SMALL_BATCH_AUTO (~(uint64_t)0)
 RAVEN_API int raven_index_set_small_batch(raven_index* ix, uint64_t max_nq);
 
 RAVEN_API const char* raven_last_error(void);

@@ -59,7 +59,7 @@ struct raven_index {
   // launch tuning
   int hash_bits_override = 0;
   int spill_bits_override = 0;
-  uint64_t small_batch_max = 0;  // batches of at most this many queries run one CTA per query
+  uint64_t small_batch_max = ~0ull;  // batches of at most this many queries run one CTA per query (~0: one wave)
 };
 
 namespace {
@@ -503,6 +503,23 @@ cudaError_t launch_cta_t(const SearchArgs& a, uint32_t smem, uint64_t nq, cudaSt
   k<<<(unsigned)nq, kCtaThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
+template <int QUANT, int CPL>
+cudaError_t occupancy_cta_t(uint32_t smem, int* per_sm) {
+  auto k = search_cta_kernel<QUANT, CPL>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k, kCtaThreads, smem);
+}
+template <int QUANT>
+cudaError_t occupancy_cta_cpl(int cpl, uint32_t smem, int* per_sm) {
+  switch (cpl) {
+    case 1: return occupancy_cta_t<QUANT, 1>(smem, per_sm);
+    case 2: return occupancy_cta_t<QUANT, 2>(smem, per_sm);
+    case 4: return occupancy_cta_t<QUANT, 4>(smem, per_sm);
+    case 8: return occupancy_cta_t<QUANT, 8>(smem, per_sm);
+  }
+  return cudaErrorInvalidValue;
+}
 template <int QUANT>
 cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, uint32_t smem, uint64_t nq, cudaStream_t st) {
   switch (cpl) {
@@ -674,7 +691,7 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
 }
 
 // Small batches: one CTA of four warps per query (search_cta.cuh), the visited
-// set in a 2^15-slot shared table; per-query global spill tables (2^13-slot
+// set in a 2^14-slot shared table; per-query global spill tables (2^13-slot
 // level A, level B 8x) stay allocated for exactness, touched only by a query
 // that fills the shared table. Same results as the batch kernel.
 int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p, const Plan& pl,
@@ -728,8 +745,16 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   if (nq == 0) return RAVEN_OK;
   if (!o || !o->ids) return fail(RAVEN_EINVAL, "outputs.ids is required");
   CU(cudaSetDevice(ix->device));
-  if (!nav_only && nq <= ix->small_batch_max && pl.quant != RAVEN_QUANT_F32 && !p->rerank_f16)
-    return run_search_cta(ix, d_q, nq, p, pl, o, st);
+  if (!nav_only && pl.quant != RAVEN_QUANT_F32 && !p->rerank_f16 && nq <= ix->small_batch_max) {
+    uint64_t lim = ix->small_batch_max;
+    if (lim == ~0ull) {  // as many queries as one wave of CTAs holds
+      int per_sm = 0;
+      const uint32_t smem = cta_smem_bytes(ix->dim_pad, ix->q_stride[pl.quant], pl.pool_cap, kCtaHashBits, ix->r_pad);
+      CU(pl.quant == 0 ? occupancy_cta_cpl<0>(pl.cpl, smem, &per_sm) : occupancy_cta_cpl<1>(pl.cpl, smem, &per_sm));
+      lim = (uint64_t)std::max(per_sm, 0) * (uint64_t)ix->num_sms;
+    }
+    if (nq <= lim) return run_search_cta(ix, d_q, nq, p, pl, o, st);
+  }
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
@@ -943,7 +968,7 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
   if (cudaDeviceGetAttribute(&ix->num_sms, cudaDevAttrMultiProcessorCount, o.device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(RAVEN_ECUDA, "device query / stream creation failed"));
-  ix->small_batch_max = (uint64_t)ix->num_sms;  // one query per SM
+  ix->small_batch_max = ~0ull;  // one wave of CTAs (resolved per call)
   {
     // per-call scratch comes from the device's stream-ordered pool; keep freed
     // blocks cached instead of returning them to the driver at every sync

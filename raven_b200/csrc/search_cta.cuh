@@ -3,10 +3,10 @@
 // A batch smaller than the GPU leaves most SMs idle under the persistent
 // one-warp-per-query kernel, and each query's latency is one warp's chain of
 // dependent expansions. Here each query gets a whole CTA:
-//   * the visited set lives in a shared-memory table of 2^15 slots (128 KB),
-//     so a query never reaches the global spill levels in practice (they
-//     remain, for exactness, behind the same capacity checks as in the batch
-//     kernel);
+//   * the visited set lives in a shared-memory table of 2^14 slots (64 KB,
+//     over 14,000 visits; three CTAs fit an SM), so a query does not reach the
+//     global spill levels in practice (they remain, for exactness, behind the
+//     same capacity checks as in the batch kernel);
 //   * the four warps share each expansion's work: every warp gathers the
 //     codes of eight of the row's neighbours and computes their distances,
 //     while warp 0 also runs the visited set and then the pool merge; the
@@ -24,7 +24,7 @@ namespace raven_dev {
 constexpr int kCtaWarps = 4;
 constexpr int kCtaThreads = 32 * kCtaWarps;
 constexpr int kCtaRowsPerWarp = 4;  // rows a warp stages per round (descent, rerank)
-constexpr uint32_t kCtaHashBits = 15;
+constexpr uint32_t kCtaHashBits = 14;
 
 // Shared memory of one query (every piece 16-byte aligned).
 struct CtaSmem {
@@ -192,7 +192,7 @@ __device__ inline bool cta_nav_descend(const SearchArgs& a, const CtaSmem& s, in
 // The small-batch kernel: grid = number of queries, kCtaThreads threads.
 // QUANT 0 (SQ4) or 1 (SQ8); f16 reranks and the f32 traversal use the batch
 // kernel. Level-A/B spill tables of query q start at a.spill + q * (9 <<
-// spill_bits) (only touched by a query that fills the 2^15-slot shared table).
+// spill_bits) (only touched by a query that fills the shared table).
 template <int QUANT, int CPL>
 __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];

@@ -26,6 +26,7 @@ import numpy as np
 from . import _lib as L
 
 SENTINEL = 0xFFFFFFFF
+SMALL_BATCH_AUTO = (1 << 64) - 1  # RAVEN_SMALL_BATCH_AUTO
 
 # Base vectors saved beside an ANNX file (`<path>.vec`), so that a saved index
 # can be loaded and searched without the caller supplying the vectors (the
@@ -200,7 +201,8 @@ class DeviceIndex:
         L.check(L.load().raven_index_set_tuning(self._h, hash_bits, spill_bits))
 
     def set_small_batch(self, max_nq: int) -> None:
-        """Batches of at most `max_nq` queries run one CTA per query (0: never)."""
+        """Batches of at most `max_nq` queries run one CTA per query (0: never;
+        SMALL_BATCH_AUTO, the default: one wave of CTAs)."""
         L.check(L.load().raven_index_set_small_batch(self._h, max_nq))
 
     def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True) -> dict:

@@ -17,6 +17,16 @@ from annx_util import annx_bytes, nav_bytes
 
 pytestmark = pytest.mark.gpu
 RTOL = 1e-5
+# Batches up to one wave of CTAs run the small-batch kernel (one CTA per
+# query), larger ones the persistent one-warp-per-query kernel; the cases
+# below run on both by switching the index's small-batch limit.
+KERNELS = ["persistent", "cta"]
+
+
+def _use(dev, path):
+    from raven_b200.index import SMALL_BATCH_AUTO
+
+    dev.set_small_batch(0 if path == "persistent" else SMALL_BATCH_AUTO)
 
 
 def _oracle_for(oracle, graph, base, sq8=True, adaptive=True):
@@ -55,12 +65,13 @@ def _compare(g, o, exact_dists=True, history=True):
             np.testing.assert_array_equal(g["history"][i, :h], o["history"][i, :h])
 
 
-@pytest.fixture(scope="module")
-def small(small_case, oracle):
+@pytest.fixture(scope="module", params=KERNELS)
+def small(request, small_case, oracle):
     from raven_b200.index import DeviceIndex
 
     base, q, g = small_case
     dev = DeviceIndex(g, base, sq4=True, sq8=True, adaptive=True)
+    _use(dev, request.param)
     oi = _oracle_for(oracle, g, base)
     return base, q, g, dev, oi
 
@@ -124,7 +135,8 @@ def test_base_vectors_find_themselves(small):
     assert np.all(got["dists"][:, 0] == 0.0)
 
 
-def test_float_data_parity_dim96(oracle, raven_lib):
+@pytest.mark.parametrize("path", KERNELS)
+def test_float_data_parity_dim96(oracle, raven_lib, path):
     """Unit-normalised floats: nav entry points and rerank depend on the
     AVX-512 summation order, which the device reproduces."""
     from raven_b200 import datasets
@@ -133,6 +145,7 @@ def test_float_data_parity_dim96(oracle, raven_lib):
     base, q = datasets.make("gmm10m-d96-unit", n=5000, nq=300)
     g = Graph.build(base, r=32, l=64, nav_m=8, seed=3)
     dev = DeviceIndex(g, base, sq4=True, sq8=True, adaptive=True)
+    _use(dev, path)
     oi = _oracle_for(oracle, g, base)
     np.testing.assert_array_equal(dev.adaptive_samples(), oi.adaptive_samples())
     for quant in (0, 1, 2):
@@ -144,7 +157,7 @@ def test_float_data_parity_dim96(oracle, raven_lib):
     _compare(got, exp)
 
 
-def _handmade(oracle, n, dim, r_max, rows, nav=None, seed=0):
+def _handmade(oracle, n, dim, r_max, rows, nav=None, seed=0, path="persistent"):
     from raven_b200.index import DeviceIndex, Graph
 
     rng = np.random.default_rng(seed)
@@ -152,28 +165,31 @@ def _handmade(oracle, n, dim, r_max, rows, nav=None, seed=0):
     b = annx_bytes(n, dim, 0, r_max, rows, nav=nav)
     g = Graph.from_bytes(b)
     dev = DeviceIndex(g, base, sq4=True, sq8=True, adaptive=nav is not None)
+    _use(dev, path)
     oi = oracle.OracleIndex(data=b)
     oi.set_vectors(base, sq4=True, sq8=True, adaptive=nav is not None)
     q = rng.integers(0, 256, size=(64, dim)).astype(np.float32)
     return base, q, dev, oi
 
 
+@pytest.mark.parametrize("path", KERNELS)
 @pytest.mark.parametrize("r_max", [20, 32, 64, 96])
-def test_degree_padding_and_wide_rows(oracle, raven_lib, r_max):
+def test_degree_padding_and_wide_rows(oracle, raven_lib, r_max, path):
     rng = np.random.default_rng(r_max)
     n, dim = 700, 32
     rows = []
     for i in range(n):
         deg = int(rng.integers(0, r_max + 1))
         rows.append([int(x) for x in rng.choice(n, size=deg, replace=False)])
-    base, q, dev, oi = _handmade(oracle, n, dim, r_max, rows)
+    base, q, dev, oi = _handmade(oracle, n, dim, r_max, rows, path=path)
     for quant in (0, 1, 2):
         got = dev.search(q, _params(ef=40, quant=quant), history_cap=2048)
         exp = oi.search(q, k=10, ef=40, rerank_factor=8, quant=quant, history_cap=2048)
         _compare(got, exp)
 
 
-def test_duplicate_ids_in_a_row(oracle, raven_lib):
+@pytest.mark.parametrize("path", KERNELS)
+def test_duplicate_ids_in_a_row(oracle, raven_lib, path):
     # The reference's visited tracker counts the first occurrence only.
     rng = np.random.default_rng(9)
     n, dim = 300, 16
@@ -181,24 +197,26 @@ def test_duplicate_ids_in_a_row(oracle, raven_lib):
     for i in range(n):
         r = [int(x) for x in rng.integers(0, n, size=24)]  # with repeats
         rows.append(r)
-    base, q, dev, oi = _handmade(oracle, n, dim, 32, rows)
+    base, q, dev, oi = _handmade(oracle, n, dim, 32, rows, path=path)
     got = dev.search(q, _params(ef=30), history_cap=1024)
     exp = oi.search(q, k=10, ef=30, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
 
 
-def test_graph_without_nav_uses_medoid(oracle, raven_lib):
+@pytest.mark.parametrize("path", KERNELS)
+def test_graph_without_nav_uses_medoid(oracle, raven_lib, path):
     rng = np.random.default_rng(4)
     n = 500
     rows = [[int(x) for x in rng.choice(n, size=16, replace=False)] for _ in range(n)]
-    base, q, dev, oi = _handmade(oracle, n, 24, 16, rows)
+    base, q, dev, oi = _handmade(oracle, n, 24, 16, rows, path=path)
     got = dev.search(q, _params(ef=20), history_cap=1024)
     exp = oi.search(q, k=10, ef=20, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
     assert np.all(got["n_nav"] == 0)
 
 
-def test_handmade_nav_with_self_padding(oracle, raven_lib):
+@pytest.mark.parametrize("path", KERNELS)
+def test_handmade_nav_with_self_padding(oracle, raven_lib, path):
     rng = np.random.default_rng(8)
     n, dim, k = 400, 16, 4
     rows = [[int(x) for x in rng.choice(n, size=12, replace=False)] for _ in range(n)]
@@ -217,7 +235,7 @@ def test_handmade_nav_with_self_padding(oracle, raven_lib):
         e2 = [int(x) for x in rng.choice(l2, size=2, replace=False)] + [u, u]
         upper[u] = upper[u] + e2
     nav = nav_bytes(0, 2, k, levels, upper, [0])
-    base, q, dev, oi = _handmade(oracle, n, dim, 12, rows, nav=nav)
+    base, q, dev, oi = _handmade(oracle, n, dim, 12, rows, nav=nav, path=path)
     got = dev.search(q, _params(ef=16), history_cap=1024)
     exp = oi.search(q, k=10, ef=16, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
@@ -411,8 +429,9 @@ def test_gmm1m_headline_parity(oracle, raven_lib):
         _compare(got, exp)
 
 
+@pytest.mark.parametrize("path", KERNELS)
 @pytest.mark.parametrize("dim", [70, 131])
-def test_odd_dim_parity(oracle, raven_lib, dim):
+def test_odd_dim_parity(oracle, raven_lib, dim, path):
     """Dims whose 16-lane chains are a multiple of 4 long but whose rows are not
     a multiple of 4 floats: staged rows are then not 16-byte aligned (scalar
     loads), descent, search and rerank must still match the oracle."""
@@ -423,6 +442,7 @@ def test_odd_dim_parity(oracle, raven_lib, dim):
     q = datasets.clustered_int(200, dim, 30, 12.0, seed=dim + 2, centre_seed=dim + 1)
     g = Graph.build(base, r=32, l=64, alpha=1.2, nav_m=8, directional=True, seed=3)
     dev = DeviceIndex(g, base, sq4=True, sq8=dim <= 128, adaptive=True)
+    _use(dev, path)
     oi = _oracle_for(oracle, g, base, sq8=dim <= 128)
     for quant in ([0, 1] if dim <= 128 else [0]):
         got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, quant=quant), history_cap=4096)

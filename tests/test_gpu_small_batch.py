@@ -1,5 +1,6 @@
 """The small-batch path (one CTA of four warps per query, search_cta.cuh),
-taken by searches of at most `small_batch_max` queries (default: one per SM),
+taken by searches of at most `small_batch_max` queries (default: one wave of
+CTAs, three per SM at dim 128),
 against the oracle on every output — ids, distances, counts, visited counts
 and order, ef used, navigation evaluations, expansions — and against the
 persistent one-warp-per-query kernel on the same queries.
@@ -65,13 +66,13 @@ def test_small_batch_spill_levels_exact(case):
 def test_small_batch_equals_persistent_kernel(case):
     base, q, dev, oi = case
     p = _params(ef=100)
-    small = dev.search(q[:100], p, history_cap=8192)
+    small = dev.search(q[:400], p, history_cap=8192)
     dev.set_small_batch(0)
     try:
-        batch = dev.search(q[:100], p, history_cap=8192)
+        batch = dev.search(q[:400], p, history_cap=8192)
     finally:
-        import torch
+        from raven_b200.index import SMALL_BATCH_AUTO
 
-        dev.set_small_batch(torch.cuda.get_device_properties(0).multi_processor_count)
+        dev.set_small_batch(SMALL_BATCH_AUTO)
     for key in small:
         np.testing.assert_array_equal(small[key], batch[key], err_msg=key)
