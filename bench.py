@@ -304,7 +304,9 @@ def parity_check(args, g, base, dev, qbatches, n_check=1000):
     public C ABI with host buffers) against the oracle on the first `n_check`
     queries of batch 0, at the bench's ef and at ef=50, on every output:
     top-k ids, result counts, visited counts, visited order, ef used,
-    navigation evaluations, expansions and the f32 rerank distances."""
+    navigation evaluations, expansions and the f32 rerank distances (exact
+    visited set), and every one of these but the visited count and order for
+    the timed mode, which runs without the visited set."""
     import tempfile
 
     from oracle import oracle as O
@@ -325,9 +327,13 @@ def parity_check(args, g, base, dev, qbatches, n_check=1000):
         params = L.SearchParams(ef=ef, k=args.k, rerank_factor=args.rr, prefetch_offset=8, quant=quant, adaptive=0,
                                 gamma=0.0, min_ef=0, max_ef=0)
         got = dev.search(q, params, history_cap=hist)
+        # the timed path: no visited counts requested, pool membership decides
+        fast = dev.search(q, params, visited=False)
         exp = oi.search(q, k=args.k, ef=ef, rerank_factor=args.rr, quant=quant, history_cap=hist,
                         threads=os.cpu_count() or 1)
         res["efs"].append(ef)
+        res["pool_membership_mode_equal"] = res.get("pool_membership_mode_equal", True) and bool(
+            all(np.array_equal(fast[k], exp[k]) for k in ("ids", "dists", "counts", "ef_used", "n_nav", "expansions")))
         res["ids_equal"] &= bool(np.array_equal(got["ids"], exp["ids"]))
         res["counts_equal"] &= bool(np.array_equal(got["counts"], exp["counts"]))
         res["visited_equal"] &= bool(np.array_equal(got["visited"], exp["visited"]))
@@ -462,8 +468,10 @@ def sharded_record(args, base, world, rank, local, steps, n_shards=SHARDED_N, n_
         oi = O.OracleIndex(paths[s])
         oi.set_vectors(parts[s], sq4=True)
         exp = oi.search(q, k=k, ef=50, rerank_factor=args.rr, threads=max(1, (os.cpu_count() or 1) // world))
-        got = shards[s].search(q, params)
+        got = shards[s].search(q, params, visited=True)
         ok &= all(np.array_equal(got[f], exp[f]) for f in ("ids", "dists", "counts", "visited"))
+        fast = shards[s].search(q, params, visited=False)  # the mode the collection's search runs in
+        ok &= all(np.array_equal(fast[f], exp[f]) for f in ("ids", "dists", "counts", "expansions"))
     ids, _, cnt = coll.search(d_q[0], params, stream)
     stream.synchronize()
     gi, gd, gc = M.read_gathered(coll.gathered(B, k, d_q.device), S, world, B, k)
@@ -674,31 +682,43 @@ def main():
                             gamma=0.0, min_ef=0, max_ef=0)
     stream = torch.cuda.Stream()
 
-    def outs(b, with_stats=True):
+    def outs(b, with_stats=True, with_visited=False):
         def p(t, ty):
             return C.cast(t[b].data_ptr(), ty)
 
         return L.SearchOutputs(
             ids=p(d_ids, L.u32p), dists=p(d_d, L.f32p),
             counts=p(stats["counts"], L.u32p) if with_stats else None,
-            visited=p(stats["visited"], L.u32p) if with_stats else None,
+            visited=p(stats["visited"], L.u32p) if with_visited else None,
             ef_used=p(stats["ef_used"], L.u32p) if with_stats else None,
             status=p(stats["status"], L.i32p) if with_stats else None,
             n_nav=p(stats["n_nav"], L.u32p) if with_stats else None,
             expansions=p(stats["expansions"], L.u32p) if with_stats else None,
             history=None, history_cap=0, history_len=None)
 
+    # the timed steps ask for no visited counts: the search decides new
+    # neighbours by pool membership (same results, no visited tables)
     out_objs = [outs(b) for b in range(nb)]
 
-    def step(i):
+    def step(i, objs=out_objs):
         b = i % nb
-        L.check(lib.raven_search_batch_device(dev._h, d_q[b].data_ptr(), B, C.byref(params), C.byref(out_objs[b]),
+        L.check(lib.raven_search_batch_device(dev._h, d_q[b].data_ptr(), B, C.byref(params), C.byref(objs[b]),
                                               stream.cuda_stream))
 
+    # untimed pass with the exact visited set: the visited counts that the
+    # algorithmic bytes are counted from, and the results both modes must share
+    vis_objs = [outs(b, with_visited=True) for b in range(nb)]
+    for b in range(nb):
+        step(b, vis_objs)
+    torch.cuda.synchronize()
+    exact_ids, exact_d = d_ids.clone(), d_d.clone()
+    exact_exp = stats["expansions"].clone()
     # warm-up (also fills stats and results for every batch)
     for i in range(max(args.warmup, nb)):
         step(i)
     torch.cuda.synchronize()
+    modes_equal = bool(torch.equal(exact_ids, d_ids) and torch.equal(exact_d, d_d)
+                       and torch.equal(exact_exp, stats["expansions"]))
 
     # recall@10 against the exact kNN kernel on all batches
     gt = torch.zeros((nb, B, k), dtype=torch.int32, device="cuda")
@@ -899,6 +919,9 @@ def main():
             "sharded": sharded,
             "recall_at_10": round(recall, 4), "queries_scored": int(got.shape[0]),
             "bad_status_queries": bad_status,
+            "visited_mode": "timed steps request no visited counts: new neighbours are decided by pool membership "
+                            "(same results); the visited counts come from an untimed pass with the exact visited set",
+            "visited_modes_equal": modes_equal,
             "avg_visited": float(st["visited"].mean()), "avg_expansions": float(st["expansions"].mean()),
             "avg_nav_evals": float(st["n_nav"].mean()),
             "l2": f"not flushed: index working set ~{(base.nbytes + base.shape[0] * (code_bytes + 4 * R)) / 2**20:.0f} "

@@ -460,39 +460,54 @@ __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float
 // ---------------------------------------------------------------------------
 // Search launch.
 // ---------------------------------------------------------------------------
-template <int QUANT, int CPL>
+template <int QUANT, int CPL, bool VIS>
 cudaError_t launch_t(const SearchArgs& a, uint32_t smem_per_block, int grid, cudaStream_t st) {
-  auto k = a.pool_cap <= 64 ? search_kernel<QUANT, CPL, 64> : search_kernel<QUANT, CPL, 0>;
+  auto k = a.pool_cap <= 64 ? search_kernel<QUANT, CPL, 64, VIS> : search_kernel<QUANT, CPL, 0, VIS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
   if (e != cudaSuccess) return e;
   k<<<grid, kWarpsPerBlock * 32, smem_per_block, st>>>(a);
   return cudaGetLastError();
 }
-template <int QUANT, int CPL>
+template <int QUANT, int CPL, bool VIS>
 cudaError_t occupancy_t(uint32_t pool_cap, uint32_t smem_per_block, int* blocks) {
-  auto k = pool_cap <= 64 ? search_kernel<QUANT, CPL, 64> : search_kernel<QUANT, CPL, 0>;
+  auto k = pool_cap <= 64 ? search_kernel<QUANT, CPL, 64, VIS> : search_kernel<QUANT, CPL, 0, VIS>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_per_block);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, k, kWarpsPerBlock * 32, smem_per_block);
 }
 
-template <int QUANT>
+template <int QUANT, bool VIS>
 cudaError_t dispatch_cpl(int cpl, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
                          int* blocks) {
   switch (cpl) {
-    case 1: return occ ? occupancy_t<QUANT, 1>(a.pool_cap, smem, blocks) : launch_t<QUANT, 1>(a, smem, grid, st);
-    case 2: return occ ? occupancy_t<QUANT, 2>(a.pool_cap, smem, blocks) : launch_t<QUANT, 2>(a, smem, grid, st);
-    case 4: return occ ? occupancy_t<QUANT, 4>(a.pool_cap, smem, blocks) : launch_t<QUANT, 4>(a, smem, grid, st);
-    case 8: return occ ? occupancy_t<QUANT, 8>(a.pool_cap, smem, blocks) : launch_t<QUANT, 8>(a, smem, grid, st);
+    case 1:
+      return occ ? occupancy_t<QUANT, 1, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 1, VIS>(a, smem, grid, st);
+    case 2:
+      return occ ? occupancy_t<QUANT, 2, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 2, VIS>(a, smem, grid, st);
+    case 4:
+      return occ ? occupancy_t<QUANT, 4, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 4, VIS>(a, smem, grid, st);
+    case 8:
+      return occ ? occupancy_t<QUANT, 8, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 8, VIS>(a, smem, grid, st);
   }
   return cudaErrorInvalidValue;
 }
-cudaError_t dispatch(int quant, int cpl, bool occ, const SearchArgs& a, uint32_t smem, int grid, cudaStream_t st,
-                     int* blocks) {
+// vis: the exact visited set (visited counts or the visited order requested,
+// or the f32 beam); otherwise pool membership decides new neighbours, with
+// the same results and no visited tables (search_kernel.cuh).
+cudaError_t dispatch(int quant, int cpl, bool vis, bool occ, const SearchArgs& a, uint32_t smem, int grid,
+                     cudaStream_t st, int* blocks) {
   if (quant == RAVEN_QUANT_F32)
-    return occ ? occupancy_t<2, 1>(a.pool_cap, smem, blocks) : launch_t<2, 1>(a, smem, grid, st);
-  return quant == 0 ? dispatch_cpl<0>(cpl, occ, a, smem, grid, st, blocks)
-                    : dispatch_cpl<1>(cpl, occ, a, smem, grid, st, blocks);
+    return occ ? occupancy_t<2, 1, true>(a.pool_cap, smem, blocks) : launch_t<2, 1, true>(a, smem, grid, st);
+  if (vis)
+    return quant == 0 ? dispatch_cpl<0, true>(cpl, occ, a, smem, grid, st, blocks)
+                      : dispatch_cpl<1, true>(cpl, occ, a, smem, grid, st, blocks);
+  return quant == 0 ? dispatch_cpl<0, false>(cpl, occ, a, smem, grid, st, blocks)
+                    : dispatch_cpl<1, false>(cpl, occ, a, smem, grid, st, blocks);
+}
+
+// Whether a batch-kernel launch needs the exact visited set.
+bool needs_visited(int quant, const raven_search_outputs* o) {
+  return quant == RAVEN_QUANT_F32 || o->visited || o->history || o->history_len;
 }
 
 template <int QUANT, int CPL>
@@ -758,14 +773,15 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
-  CU(dispatch(pl.quant, pl.cpl, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
+  const bool vis = nav_only || needs_visited(pl.quant, o);
+  CU(dispatch(pl.quant, pl.cpl, vis, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
   if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
   uint64_t grid64 = (uint64_t)blocks_per_sm * ix->num_sms;
   uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
   int grid = (int)std::max<uint64_t>(1, std::min(grid64, need));
   const uint64_t slots = (uint64_t)grid * kWarpsPerBlock;
-  // per-call scratch: work counter, spill tables, ef table (stream ordered)
-  const size_t spill_bytes = (size_t)slots * (9ull << pl.spill_bits) * 4;  // levels A + B per slot
+  // per-call scratch: work counter, spill tables (exact visited set only), ef table (stream ordered)
+  const size_t spill_bytes = vis && !nav_only ? (size_t)slots * (9ull << pl.spill_bits) * 4 : 0;  // levels A + B
   const size_t table_bytes = pl.table.size() * 4;
   size_t total = 256 + spill_bytes + ((table_bytes + 255) & ~(size_t)255);
   uint8_t* scratch = nullptr;
@@ -783,14 +799,14 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   SearchArgs a{};
   fill_args(ix, pl, p, o, &a);
   a.ef_table = table;
-  a.spill = spill;
+  a.spill = spill_bytes ? spill : nullptr;
   a.n_slots = slots;
   a.queries = d_q;
   a.nq = nq;
   a.rerank_f16 = (!nav_only && p->rerank_f16) ? 1 : 0;
   a.counter = counter;
   a.nav_only = nav_only;
-  e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
+  e = dispatch(pl.quant, pl.cpl, vis, false, a, pl.smem_block, grid, st, nullptr);
   cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
   return RAVEN_OK;
@@ -1558,10 +1574,14 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
-  CU(dispatch(pl.quant, pl.cpl, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
+  // without visited counts or the visited order the search keeps no visited
+  // tables, and the array holds only the counter and the ef table
+  const bool vis = needs_visited(pl.quant, o);
+  CU(dispatch(pl.quant, pl.cpl, vis, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
   if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
   const uint64_t need = (nq + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  const uint64_t grid64 = std::min<uint64_t>({(uint64_t)blocks_per_sm * ix->num_sms, need, max_slots / kWarpsPerBlock});
+  const uint64_t grid64 = std::min<uint64_t>(
+      {(uint64_t)blocks_per_sm * ix->num_sms, need, vis ? max_slots / kWarpsPerBlock : ~0ull});
   if (grid64 == 0) return fail(RAVEN_ELIMIT, "fixed scratch array too small for one block of spill tables");
   const int grid = (int)grid64;
   const uint64_t slots = (uint64_t)grid * kWarpsPerBlock;
@@ -1577,13 +1597,13 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   fill_args(ix, pl, p, o, &a);
   a.ef_table = table;
   a.spill_bits = sb;
-  a.spill = spill;
+  a.spill = vis ? spill : nullptr;
   a.n_slots = slots;
   a.queries = d_q;
   a.nq = nq;
   a.counter = counter;
   a.nav_only = 0;
-  const cudaError_t e = dispatch(pl.quant, pl.cpl, false, a, pl.smem_block, grid, st, nullptr);
+  const cudaError_t e = dispatch(pl.quant, pl.cpl, vis, false, a, pl.smem_block, grid, st, nullptr);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
   return RAVEN_OK;
 }

@@ -16,6 +16,20 @@
 // the build's greedy_search_vec_build, :530-567). With f32 distances there is
 // no query code and no rerank: the result is the first k entries of the pool.
 //
+// VIS selects how step 4 decides that a neighbour is new. true: an exact
+// visited set (VisitedTracker), which the visited count, the visited order
+// and the f32 beam need. false (SQ4/SQ8 only): membership in the pool. Every
+// visited node that is not in the pool has a distance >= the pool's current
+// worst entry once the pool is full (it was rejected at or above an earlier
+// worst, or evicted from the last slot, and the worst never rises), and while
+// the pool is not full every visited node is in it. So "not visited" and "not
+// in the pool" accept exactly the same candidates, and ids, distances,
+// expansion order and every other result are unchanged; a visited neighbour
+// that the pool has dropped is merely scored again (its code was gathered
+// anyway) and rejected. The duplicate test costs one shared read after the
+// binary search that places the candidate: an equal id can only sit in the
+// run of equal distances just before its slot.
+//
 // LinearPool equivalence used by the batch merge: the pool always holds the
 // first `ef` of all inserted candidates ordered by (distance, insertion order)
 // and the cursor is the first unexpanded entry. A new candidate therefore loses
@@ -669,8 +683,9 @@ struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
 // ---------------------------------------------------------------------------
 // POOLMAX: 64 for pools of at most 64 entries (layout and merge bounds fixed
 // at compile time), 0 for a run-time capacity (a.pool_cap).
-template <int QUANT, int CPL, int POOLMAX>
+template <int QUANT, int CPL, int POOLMAX, bool VIS>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_kernel(const SearchArgs a) {
+  static_assert(VIS || QUANT != 2, "the f32 beam scores new neighbours only: it needs the visited set");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -787,18 +802,22 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
                                                      a.levels)
                                  : (uint8_t)0;
       }
-      // clear the visited table (the staging rows of the descent are done)
-      for (uint32_t i = lane * 4; i < H; i += 128) *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-      __syncwarp();
+      if (VIS) {
+        // clear the visited table (the staging rows of the descent are done)
+        for (uint32_t i = lane * 4; i < H; i += 128) *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+        __syncwarp();
+      }
       QChunk<QUANT> qc;
       qc.load(s.qcode, sub);
 
       int level = 0;
       uint32_t tcount = 0, scount = 0;
       // 4. entry
-      if (lane == 0) shared_insert2(s.ht, a.hash_bits - 2, entry);
-      tcount = 1;
-      if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
+      if (VIS) {
+        if (lane == 0) shared_insert2(s.ht, a.hash_bits - 2, entry);
+        tcount = 1;
+        if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
+      }
       vcount = 1;
       if (QUANT == 2) {
         // l2_simd(query, vectors[entry]) (src/graph/vamana.rs:603-606); non-negative
@@ -884,33 +903,11 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
           // rows hold no repeated id (the upload drops later repeats, which the
           // reference treats as already visited), so every valid lane probes.
           const bool valid = lane < deg;
-          // visited-set level: 0 shared table, 1 spill A, 2 spill B
-          if (level == 0 && tcount + 32 > h_limit) {
-            if (spill == nullptr) {
-              overflow = true;
-              break;
-            }
-            for (uint32_t i = lane * 4; i < S; i += 128)
-              *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-            __syncwarp();
-            level = 1;
-          } else if (level == 1 && scount + 32 > s_limit) {
-            for (uint32_t i = lane * 4; i < SB; i += 128)
-              *(uint4*)(spill_b + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-            __syncwarp();
-            level = 2;
-            scount = 0;
-          } else if (level == 2 && scount + 32 > sb_limit) {
-            overflow = true;
-            break;
-          }
           bool is_new = false;
-          // every id lives in exactly one level; insert into the current one
-          if (level == 0) {
-            const int r = valid ? shared_insert2(s.ht, a.hash_bits - 2, id) : 0;
-            is_new = r == 1;
-            const bool to_spill = r == 3;  // both buckets full: this id starts level A
-            if (__any_sync(kFull, to_spill)) {
+          uint32_t newm = 0;  // lanes holding a first visit
+          if (VIS) {
+            // visited-set level: 0 shared table, 1 spill A, 2 spill B
+            if (level == 0 && tcount + 32 > h_limit) {
               if (spill == nullptr) {
                 overflow = true;
                 break;
@@ -919,39 +916,64 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
                 *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
               __syncwarp();
               level = 1;
-              const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
-              const uint4 sv = to_spill ? __ldcv((const uint4*)(spill + 4 * sbk)) : make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-              is_new |= spill_insert_warp(spill, a.spill_bits, id, to_spill, sbk, sv, lane);
+            } else if (level == 1 && scount + 32 > s_limit) {
+              for (uint32_t i = lane * 4; i < SB; i += 128)
+                *(uint4*)(spill_b + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+              __syncwarp();
+              level = 2;
+              scount = 0;
+            } else if (level == 2 && scount + 32 > sb_limit) {
+              overflow = true;
+              break;
             }
-          } else if (level == 1) {
-            // home bucket of level A read before the shared lookup: the two overlap
-            const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
-            uint4 sv = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-            if (valid) sv = __ldcv((const uint4*)(spill + 4 * sbk));
-            const bool need = valid && !shared_has2(s.ht, a.hash_bits - 2, id);
-            is_new = spill_insert_warp(spill, a.spill_bits, id, need, sbk, sv, lane);
-          } else if (valid && !shared_has2(s.ht, a.hash_bits - 2, id)) {
-            is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
+            // every id lives in exactly one level; insert into the current one
+            if (level == 0) {
+              const int r = valid ? shared_insert2(s.ht, a.hash_bits - 2, id) : 0;
+              is_new = r == 1;
+              const bool to_spill = r == 3;  // both buckets full: this id starts level A
+              if (__any_sync(kFull, to_spill)) {
+                if (spill == nullptr) {
+                  overflow = true;
+                  break;
+                }
+                for (uint32_t i = lane * 4; i < S; i += 128)
+                  *(uint4*)(spill + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+                __syncwarp();
+                level = 1;
+                const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
+                const uint4 sv = to_spill ? __ldcv((const uint4*)(spill + 4 * sbk)) : make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+                is_new |= spill_insert_warp(spill, a.spill_bits, id, to_spill, sbk, sv, lane);
+              }
+            } else if (level == 1) {
+              // home bucket of level A read before the shared lookup: the two overlap
+              const uint32_t sbk = hash_slot(id, a.spill_bits - 2);
+              uint4 sv = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+              if (valid) sv = __ldcv((const uint4*)(spill + 4 * sbk));
+              const bool need = valid && !shared_has2(s.ht, a.hash_bits - 2, id);
+              is_new = spill_insert_warp(spill, a.spill_bits, id, need, sbk, sv, lane);
+            } else if (valid && !shared_has2(s.ht, a.hash_bits - 2, id)) {
+              is_new = probe_level_b(spill, spill_b, a.spill_bits, id);
+            }
+            newm = __ballot_sync(kFull, is_new);
+            if (newm == 0) continue;
+            const int nn = __popc(newm);
+            if (level == 0) tcount += nn;
+            else scount += nn;
+            if (a.history && is_new) {
+              const uint32_t pos = vcount + __popc(newm & lanemask_lt(lane));
+              if (pos < a.hist_cap) a.history[qi * a.hist_cap + pos] = id;
+            }
+            vcount += nn;
           }
-          const uint32_t newm = __ballot_sync(kFull, is_new);
-          const int nn = __popc(newm);
-          if (nn == 0) continue;
-          if (level == 0) tcount += nn;
-          else scount += nn;
-          if (a.history && is_new) {
-            const uint32_t pos = vcount + __popc(newm & lanemask_lt(lane));
-            if (pos < a.hist_cap) a.history[qi * a.hist_cap + pos] = id;
-          }
-          vcount += nn;
           uint32_t my_d;
-          if (QUANT == 2) {
+          if constexpr (QUANT == 2) {
             // f32 distances of the new neighbours only, in adjacency order
             // (compacted), their rows staged in shared memory
             const int cpos = __popc(newm & lanemask_lt(lane));
             if (is_new) s.cand_id[cpos] = id;
             __syncwarp();
-            rows_dist(s.qf, s.fstage, a.f32_stage_rows, s.cand_id, nn, a.dim, a.vec_c, a.vec_rem, vec_row, s.nd,
-                      lane);
+            rows_dist(s.qf, s.fstage, a.f32_stage_rows, s.cand_id, __popc(newm), a.dim, a.vec_c, a.vec_rem, vec_row,
+                      s.nd, lane);
             my_d = is_new ? __float_as_uint(s.nd[cpos]) : 0xffffffffu;
           } else {
             // integer distances of the row (candidate idx -> cand_d[idx])
@@ -966,20 +988,38 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
               }
             }
             __syncwarp();
-            my_d = is_new ? s.cand_d[lane] : 0xffffffffu;
+            my_d = (VIS ? is_new : valid) ? s.cand_d[lane] : 0xffffffffu;
           }
           // merge the new neighbours (adjacency order) into the pool:
           // LinearPool::insert semantics, batched
           const bool full = sz == (int)ef;
           const uint32_t worst = full ? s.pool_d[sz - 1] : 0xffffffffu;
-          const bool acc = is_new && (!full || my_d < worst);
+          bool acc = (VIS ? is_new : valid) && (!full || my_d < worst);
+          int slot_lo = 0;  // without the visited set: # pool entries <= my_d
+          if (!VIS && acc) {
+            int lo = 0, hi = sz;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (s.pool_d[mid] <= my_d) lo = mid + 1;
+              else hi = mid;
+            }
+            slot_lo = lo;
+            // already in the pool: an equal id sits in the run of equal
+            // distances ending at lo - 1
+            for (int j = lo - 1; j >= 0 && s.pool_d[j] == my_d; --j)
+              if ((s.pool_id[j] & ~kChecked) == id) {
+                acc = false;
+                break;
+              }
+          }
           const uint32_t am = __ballot_sync(kFull, acc);
           const int na = __popc(am);
           __syncwarp();
           if (na > 0) {
             // pool entries from the first insertion point onward move right
             int cpos = 0x7fffffff;
-            if (acc) {
+            if (acc && !VIS) cpos = slot_lo;
+            if (acc && VIS) {
               int lo = 0, hi = sz;  // # pool entries <= my_d (ties: pool first)
               while (lo < hi) {
                 const int mid = (lo + hi) >> 1;
@@ -1120,12 +1160,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
     }
     if (lane == 0) {
       if (a.counts) a.counts[qi] = (uint32_t)kout;
-      if (a.visited) a.visited[qi] = vcount;
+      if (VIS && a.visited) a.visited[qi] = vcount;
       if (a.ef_used) a.ef_used[qi] = ef;
       if (a.status) a.status[qi] = status;
       if (a.n_nav) a.n_nav[qi] = n_nav;
       if (a.expansions) a.expansions[qi] = expansions;
-      if (a.hist_len) a.hist_len[qi] = vcount;
+      if (VIS && a.hist_len) a.hist_len[qi] = vcount;
     }
     __syncwarp();
   }

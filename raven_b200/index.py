@@ -205,8 +205,13 @@ class DeviceIndex:
         SMALL_BATCH_AUTO, the default: one wave of CTAs)."""
         L.check(L.load().raven_index_set_small_batch(self._h, max_nq))
 
-    def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True) -> dict:
-        """Host-buffer batch search (raven_search_batch). Returns a dict of arrays."""
+    def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True,
+               visited: Optional[bool] = None) -> dict:
+        """Host-buffer batch search (raven_search_batch). Returns a dict of arrays.
+
+        `stats` adds ef_used, status, n_nav and expansions; `visited` (default:
+        with the history) adds the per-query visited count, which runs the
+        search with the exact visited set; results are the same either way."""
         q = _f32c(queries)
         if q.ndim == 1:
             q = q[None, :]
@@ -219,9 +224,11 @@ class DeviceIndex:
             "counts": np.zeros(nq, dtype=np.uint32),
         }
         if stats:
-            for name, dt in (("visited", np.uint32), ("ef_used", np.uint32), ("status", np.int32),
-                             ("n_nav", np.uint32), ("expansions", np.uint32)):
+            for name, dt in (("ef_used", np.uint32), ("status", np.int32), ("n_nav", np.uint32),
+                             ("expansions", np.uint32)):
                 res[name] = np.zeros(nq, dtype=dt)
+        if visited or (visited is None and history_cap):
+            res["visited"] = np.zeros(nq, dtype=np.uint32)
         if history_cap:
             res["history"] = np.zeros((nq, history_cap), dtype=np.uint32)
             res["history_len"] = np.zeros(nq, dtype=np.uint32)
@@ -329,11 +336,13 @@ class GraphSearcher:
             p.max_ef = self._adaptive.max_ef
         return p
 
-    def _search(self, queries, k: int, quant: int):
+    def _search(self, queries, k: int, quant: int, visited: bool = True):
         if quant != L.RAVEN_QUANT_F32 and not self._want["sq4" if quant == L.RAVEN_QUANT_SQ4 else "sq8"]:
             name = "sq4" if quant == L.RAVEN_QUANT_SQ4 else "sq8"
             raise RuntimeError(f"search_{name} requires with_{name}() first")
-        return self._device_index().search(queries, self._params(k, quant))
+        # single-query calls keep last_visited_count (the exact visited set);
+        # batch_search has no such diagnostic and runs without it
+        return self._device_index().search(queries, self._params(k, quant), visited=visited)
 
     def search(self, query, k: int) -> List[Tuple[int, float]]:
         """GraphSearcher::search (src/graph/vamana.rs:1627-1672): the beam over
@@ -364,7 +373,7 @@ class GraphSearcher:
         quant = (L.RAVEN_QUANT_SQ8 if self._want["sq8"] else
                  L.RAVEN_QUANT_SQ4 if self._want["sq4"] else L.RAVEN_QUANT_F32)
         q = _f32c(queries)
-        r = self._search(q, k, quant)
+        r = self._search(q, k, quant, visited=False)
         return [[(int(i), float(d)) for i, d in zip(r["ids"][j, : r["counts"][j]], r["dists"][j, : r["counts"][j]])]
                 for j in range(q.shape[0])]
 
@@ -396,7 +405,6 @@ class Searcher:
         self.cur_gamma, self.cur_min_ef, self.cur_max_ef = 2.0, 30, 100
         self._dev = DeviceIndex(graph, vectors, device=device, sq4=self._quant == L.RAVEN_QUANT_SQ4,
                                 sq8=self._quant == L.RAVEN_QUANT_SQ8, adaptive=adaptive)
-        self.last_visited_count = 0
         self.last_ef_used = self.ef
 
     @property
@@ -428,7 +436,6 @@ class Searcher:
         if q.shape[0] != self.dim:
             raise ValueError(f"dim mismatch: expected {self.dim}, got {q.shape[0]}")
         r = self._dev.search(q[None, :], self.params(k))
-        self.last_visited_count = int(r["visited"][0])
         self.last_ef_used = int(r["ef_used"][0])
         return r["ids"][0, : r["counts"][0]].astype(np.uintp)
 

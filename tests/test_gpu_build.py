@@ -68,7 +68,7 @@ def test_gpu_build_equals_host_build(data, oracle):
     dev = DeviceIndex(gpu, base, sq4=True)
     p = L.SearchParams(ef=50, k=10, rerank_factor=8, prefetch_offset=8, quant=0, adaptive=0, gamma=0.0, min_ef=0,
                        max_ef=0)
-    got = dev.search(q, p)
+    got = dev.search(q, p, visited=True)
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "g.annx")
         gpu.save(path)

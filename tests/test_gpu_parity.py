@@ -14,6 +14,7 @@ import numpy as np
 import pytest
 
 from annx_util import annx_bytes, nav_bytes
+from search_check import search_both
 
 pytestmark = pytest.mark.gpu
 RTOL = 1e-5
@@ -92,7 +93,7 @@ def test_adaptive_samples_match_oracle(small):
                                      (200, 10, 8)])
 def test_search_sq4_parity(small, ef, k, rr):
     base, q, g, dev, oi = small
-    got = dev.search(q, _params(ef=ef, k=k, rerank_factor=rr), history_cap=4096)
+    got = search_both(dev, q, _params(ef=ef, k=k, rerank_factor=rr), history_cap=4096)
     exp = oi.search(q, k=k, ef=ef, rerank_factor=rr, quant=0, history_cap=4096)
     _compare(got, exp)
 
@@ -104,7 +105,7 @@ def test_search_f32_parity(small, ef, k):
     from raven_b200 import _lib as L
 
     base, q, g, dev, oi = small
-    got = dev.search(q, _params(ef=ef, k=k, quant=L.RAVEN_QUANT_F32), history_cap=4096)
+    got = search_both(dev, q, _params(ef=ef, k=k, quant=L.RAVEN_QUANT_F32), history_cap=4096)
     exp = oi.search(q, k=k, ef=ef, quant=2, history_cap=4096)
     _compare(got, exp)
 
@@ -112,7 +113,7 @@ def test_search_f32_parity(small, ef, k):
 @pytest.mark.parametrize("ef", [40, 50, 100])
 def test_search_sq8_parity(small, ef):
     base, q, g, dev, oi = small
-    got = dev.search(q, _params(ef=ef, quant=1), history_cap=4096)
+    got = search_both(dev, q, _params(ef=ef, quant=1), history_cap=4096)
     exp = oi.search(q, k=10, ef=ef, rerank_factor=8, quant=1, history_cap=4096)
     _compare(got, exp)
 
@@ -120,7 +121,7 @@ def test_search_sq8_parity(small, ef):
 @pytest.mark.parametrize("gamma,lo,hi", [(2.0, 35, 65), (2.4, 35, 75), (3.5, 35, 85), (1.0, 10, 10)])
 def test_adaptive_ef_parity(small, gamma, lo, hi):
     base, q, g, dev, oi = small
-    got = dev.search(q, _params(adaptive=1, gamma=gamma, min_ef=lo, max_ef=hi), history_cap=4096)
+    got = search_both(dev, q, _params(adaptive=1, gamma=gamma, min_ef=lo, max_ef=hi), history_cap=4096)
     exp = oi.search(q, k=10, rerank_factor=8, adaptive=True, gamma=gamma, min_ef=lo, max_ef=hi, history_cap=4096)
     _compare(got, exp)
     assert got["ef_used"].min() >= max(lo, 10) or lo < 10
@@ -130,7 +131,7 @@ def test_base_vectors_find_themselves(small):
     # src/graph/vamana.rs:2169-2191: the query itself ranks first.
     base, q, g, dev, oi = small
     idx = np.arange(0, base.shape[0], 97)
-    got = dev.search(base[idx], _params(ef=50, k=5))
+    got = search_both(dev, base[idx], _params(ef=50, k=5))
     np.testing.assert_array_equal(got["ids"][:, 0], idx)
     assert np.all(got["dists"][:, 0] == 0.0)
 
@@ -149,10 +150,10 @@ def test_float_data_parity_dim96(oracle, raven_lib, path):
     oi = _oracle_for(oracle, g, base)
     np.testing.assert_array_equal(dev.adaptive_samples(), oi.adaptive_samples())
     for quant in (0, 1, 2):
-        got = dev.search(q, _params(ef=50, quant=quant), history_cap=4096)
+        got = search_both(dev, q, _params(ef=50, quant=quant), history_cap=4096)
         exp = oi.search(q, k=10, ef=50, rerank_factor=8, quant=quant, history_cap=4096)
         _compare(got, exp, exact_dists=True)
-    got = dev.search(q, _params(adaptive=1, gamma=2.0, min_ef=35, max_ef=75), history_cap=4096)
+    got = search_both(dev, q, _params(adaptive=1, gamma=2.0, min_ef=35, max_ef=75), history_cap=4096)
     exp = oi.search(q, k=10, rerank_factor=8, adaptive=True, gamma=2.0, min_ef=35, max_ef=75, history_cap=4096)
     _compare(got, exp)
 
@@ -183,7 +184,7 @@ def test_degree_padding_and_wide_rows(oracle, raven_lib, r_max, path):
         rows.append([int(x) for x in rng.choice(n, size=deg, replace=False)])
     base, q, dev, oi = _handmade(oracle, n, dim, r_max, rows, path=path)
     for quant in (0, 1, 2):
-        got = dev.search(q, _params(ef=40, quant=quant), history_cap=2048)
+        got = search_both(dev, q, _params(ef=40, quant=quant), history_cap=2048)
         exp = oi.search(q, k=10, ef=40, rerank_factor=8, quant=quant, history_cap=2048)
         _compare(got, exp)
 
@@ -198,7 +199,7 @@ def test_duplicate_ids_in_a_row(oracle, raven_lib, path):
         r = [int(x) for x in rng.integers(0, n, size=24)]  # with repeats
         rows.append(r)
     base, q, dev, oi = _handmade(oracle, n, dim, 32, rows, path=path)
-    got = dev.search(q, _params(ef=30), history_cap=1024)
+    got = search_both(dev, q, _params(ef=30), history_cap=1024)
     exp = oi.search(q, k=10, ef=30, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
 
@@ -209,7 +210,7 @@ def test_graph_without_nav_uses_medoid(oracle, raven_lib, path):
     n = 500
     rows = [[int(x) for x in rng.choice(n, size=16, replace=False)] for _ in range(n)]
     base, q, dev, oi = _handmade(oracle, n, 24, 16, rows, path=path)
-    got = dev.search(q, _params(ef=20), history_cap=1024)
+    got = search_both(dev, q, _params(ef=20), history_cap=1024)
     exp = oi.search(q, k=10, ef=20, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
     assert np.all(got["n_nav"] == 0)
@@ -236,20 +237,20 @@ def test_handmade_nav_with_self_padding(oracle, raven_lib, path):
         upper[u] = upper[u] + e2
     nav = nav_bytes(0, 2, k, levels, upper, [0])
     base, q, dev, oi = _handmade(oracle, n, dim, 12, rows, nav=nav, path=path)
-    got = dev.search(q, _params(ef=16), history_cap=1024)
+    got = search_both(dev, q, _params(ef=16), history_cap=1024)
     exp = oi.search(q, k=10, ef=16, rerank_factor=8, history_cap=1024)
     _compare(got, exp)
-    got = dev.search(q, _params(adaptive=1, gamma=2.0, min_ef=8, max_ef=30), history_cap=1024)
+    got = search_both(dev, q, _params(adaptive=1, gamma=2.0, min_ef=8, max_ef=30), history_cap=1024)
     exp = oi.search(q, k=10, rerank_factor=8, adaptive=True, gamma=2.0, min_ef=8, max_ef=30, history_cap=1024)
     _compare(got, exp)
 
 
 def test_empty_batch_and_padding(small):
     base, q, g, dev, oi = small
-    r = dev.search(q[:0], _params())
+    r = search_both(dev, q[:0], _params())
     assert r["ids"].shape == (0, 10)
     # k larger than the pool: fewer results, zero padding (src/python.rs:344-349)
-    got = dev.search(q[:20], _params(ef=4, k=10, rerank_factor=1))
+    got = search_both(dev, q[:20], _params(ef=4, k=10, rerank_factor=1))
     exp = oi.search(q[:20], k=10, ef=4, rerank_factor=1)
     np.testing.assert_array_equal(got["counts"], exp["counts"])
     assert np.all(got["counts"] == 4)
@@ -264,7 +265,7 @@ def test_nan_and_extreme_queries(small):
     qq[1, :] = 1e30
     qq[2, :] = -1e30
     qq[3, :] = 0.0
-    got = dev.search(qq, _params(), history_cap=4096)
+    got = search_both(dev, qq, _params(), history_cap=4096)
     exp = oi.search(qq, k=10, ef=50, rerank_factor=8, history_cap=4096)
     np.testing.assert_array_equal(got["ids"], exp["ids"])
     np.testing.assert_array_equal(got["visited"], exp["visited"])
@@ -279,16 +280,16 @@ def test_errors_are_status_codes(small):
 
     base, q, g, dev, oi = small
     with pytest.raises(L.RavenError) as e:
-        dev.search(q[:2], _params(ef=0))
+        search_both(dev, q[:2], _params(ef=0))
     assert e.value.code == L.RAVEN_EINVAL
     with pytest.raises(L.RavenError) as e:
-        dev.search(q[:2], _params(ef=300))
+        search_both(dev, q[:2], _params(ef=300))
     assert e.value.code == L.RAVEN_ELIMIT
     with pytest.raises(L.RavenError) as e:
-        dev.search(q[:2], _params(k=0))
+        search_both(dev, q[:2], _params(k=0))
     assert e.value.code == L.RAVEN_EINVAL
     with pytest.raises(L.RavenError) as e:
-        dev.search(q[:2], _params(adaptive=1, min_ef=50, max_ef=10))
+        search_both(dev, q[:2], _params(adaptive=1, min_ef=50, max_ef=10))
     assert e.value.code == L.RAVEN_EINVAL
 
 
@@ -299,7 +300,7 @@ def test_quantiser_not_uploaded_is_state_error(small_case, raven_lib):
     base, q, g = small_case
     dev = DeviceIndex(g, base, sq4=True, sq8=False)
     with pytest.raises(L.RavenError) as e:
-        dev.search(q[:2], _params(quant=1))
+        search_both(dev, q[:2], _params(quant=1))
     assert e.value.code == L.RAVEN_ESTATE
 
 
@@ -311,7 +312,7 @@ def test_small_visited_table_spills_exactly(small, hash_bits, spill_bits, ef):
     base, q, g, dev, oi = small
     dev.set_tuning(hash_bits=hash_bits, spill_bits=spill_bits)
     try:
-        got = dev.search(q, _params(ef=ef), history_cap=8192)
+        got = search_both(dev, q, _params(ef=ef), history_cap=8192)
         exp = oi.search(q, k=10, ef=ef, rerank_factor=8, history_cap=8192)
         _compare(got, exp)
         if spill_bits:
@@ -335,7 +336,7 @@ def test_device_entry_point_matches_host_entry(small):
     L.check(L.load().raven_search_batch_device(dev._h, qt.data_ptr(), nq, C.byref(_params()), C.byref(out),
                                                st.cuda_stream))
     torch.cuda.synchronize()
-    host = dev.search(q, _params())
+    host = search_both(dev, q, _params())
     np.testing.assert_array_equal(ids.cpu().numpy().view(np.uint32), host["ids"])
     np.testing.assert_array_equal(ds.cpu().numpy(), host["dists"])
 
@@ -398,7 +399,7 @@ def test_gmm100k_full_parity(oracle, raven_lib):
     g = datasets.load_or_build("gmm100k-d128", base=base)
     dev = DeviceIndex(g, base, sq4=True, sq8=False, adaptive=True)
     oi = _oracle_for(oracle, g, base, sq8=False)
-    got = dev.search(q, _params(ef=50, k=10, rerank_factor=8), history_cap=4096)
+    got = search_both(dev, q, _params(ef=50, k=10, rerank_factor=8), history_cap=4096)
     exp = oi.search(q, k=10, ef=50, rerank_factor=8, history_cap=4096)
     _compare(got, exp)
     gi, _ = oracle.bruteforce(base, q[:1000], 10)
@@ -422,9 +423,9 @@ def test_gmm1m_headline_parity(oracle, raven_lib):
     dev = DeviceIndex(g, base, sq4=True)
     oi = _oracle_for(oracle, g, base, sq8=False, adaptive=False)
     for ef in (50, 140):
-        full = dev.search(q, _params(ef=ef))
+        full = search_both(dev, q, _params(ef=ef))
         assert np.all(full["status"] == 0)
-        got = dev.search(q[:2000], _params(ef=ef), history_cap=8192)
+        got = search_both(dev, q[:2000], _params(ef=ef), history_cap=8192)
         exp = oi.search(q[:2000], k=10, ef=ef, rerank_factor=8, history_cap=8192)
         _compare(got, exp)
 
@@ -445,7 +446,7 @@ def test_odd_dim_parity(oracle, raven_lib, dim, path):
     _use(dev, path)
     oi = _oracle_for(oracle, g, base, sq8=dim <= 128)
     for quant in ([0, 1] if dim <= 128 else [0]):
-        got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, quant=quant), history_cap=4096)
+        got = search_both(dev, q, _params(ef=50, k=10, rerank_factor=8, quant=quant), history_cap=4096)
         exp = oi.search(q, k=10, ef=50, rerank_factor=8, quant=quant, history_cap=4096)
         _compare(got, exp)
 
@@ -464,7 +465,7 @@ def test_f16_rerank_parity(oracle, raven_lib, dim):
     dev = DeviceIndex(g, base, sq4=True, f16=True)
     oi = _oracle_for(oracle, g, base, sq8=False, adaptive=False)
     oi.set_vectors(base, sq4=True, f16=True)
-    got = dev.search(q, _params(ef=50, k=10, rerank_factor=8, rerank_f16=1), history_cap=4096)
+    got = search_both(dev, q, _params(ef=50, k=10, rerank_factor=8, rerank_f16=1), history_cap=4096)
     exp = oi.search(q, k=10, ef=50, rerank_factor=8, history_cap=4096, rerank_f16=True)
     _compare(got, exp)
     f32 = oi.search(q, k=10, ef=50, rerank_factor=8)

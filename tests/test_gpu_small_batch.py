@@ -10,6 +10,7 @@ import tempfile
 
 import numpy as np
 import pytest
+from search_check import search_both
 
 from test_gpu_parity import _compare, _params
 
@@ -34,17 +35,17 @@ def case(small_case, oracle):
 @pytest.mark.parametrize("ef,k,rr", [(50, 10, 8), (140, 10, 8), (1, 1, 1), (200, 32, 2)])
 def test_small_batch_sq4_parity(case, nq, ef, k, rr):
     base, q, dev, oi = case
-    got = dev.search(q[:nq], _params(ef=ef, k=k, rerank_factor=rr), history_cap=8192)
+    got = search_both(dev, q[:nq], _params(ef=ef, k=k, rerank_factor=rr), history_cap=8192)
     exp = oi.search(q[:nq], k=k, ef=ef, rerank_factor=rr, history_cap=8192)
     _compare(got, exp)
 
 
 def test_small_batch_sq8_and_adaptive_parity(case):
     base, q, dev, oi = case
-    got = dev.search(q[:64], _params(ef=60, quant=1), history_cap=8192)
+    got = search_both(dev, q[:64], _params(ef=60, quant=1), history_cap=8192)
     exp = oi.search(q[:64], k=10, ef=60, rerank_factor=8, quant=1, history_cap=8192)
     _compare(got, exp)
-    got = dev.search(q[:64], _params(adaptive=1, gamma=2.4, min_ef=35, max_ef=75), history_cap=8192)
+    got = search_both(dev, q[:64], _params(adaptive=1, gamma=2.4, min_ef=35, max_ef=75), history_cap=8192)
     exp = oi.search(q[:64], k=10, rerank_factor=8, adaptive=True, gamma=2.4, min_ef=35, max_ef=75, history_cap=8192)
     _compare(got, exp)
 
@@ -55,7 +56,7 @@ def test_small_batch_spill_levels_exact(case):
     base, q, dev, oi = case
     dev.set_tuning(hash_bits=8, spill_bits=10)
     try:
-        got = dev.search(q[:64], _params(ef=200), history_cap=8192)
+        got = search_both(dev, q[:64], _params(ef=200), history_cap=8192)
     finally:
         dev.set_tuning(hash_bits=0, spill_bits=0)
     exp = oi.search(q[:64], k=10, ef=200, rerank_factor=8, history_cap=8192)
@@ -66,10 +67,10 @@ def test_small_batch_spill_levels_exact(case):
 def test_small_batch_equals_persistent_kernel(case):
     base, q, dev, oi = case
     p = _params(ef=100)
-    small = dev.search(q[:400], p, history_cap=8192)
+    small = search_both(dev, q[:400], p, history_cap=8192)
     dev.set_small_batch(0)
     try:
-        batch = dev.search(q[:400], p, history_cap=8192)
+        batch = search_both(dev, q[:400], p, history_cap=8192)
     finally:
         from raven_b200.index import SMALL_BATCH_AUTO
 

@@ -22,7 +22,7 @@ RTOL = 1e-5  # the f32 rerank tolerance used by the parity tests
 HIST = 8192
 
 
-def _run(lib, L, fn, dev, q, params):
+def _run(lib, L, fn, dev, q, params, visited=True):
     import torch
 
     nq, k = q.shape[0], params.k
@@ -34,11 +34,13 @@ def _run(lib, L, fn, dev, q, params):
     hist = torch.zeros((nq, HIST), dtype=torch.int32, device="cuda")
     out = L.SearchOutputs(ids=C.cast(ids.data_ptr(), L.u32p), dists=C.cast(ds.data_ptr(), L.f32p),
                           counts=C.cast(stats["counts"].data_ptr(), L.u32p),
-                          visited=C.cast(stats["visited"].data_ptr(), L.u32p),
                           ef_used=C.cast(stats["ef_used"].data_ptr(), L.u32p),
-                          status=C.cast(stats["status"].data_ptr(), L.i32p),
-                          history=C.cast(hist.data_ptr(), L.u32p), history_cap=HIST,
-                          history_len=C.cast(stats["history_len"].data_ptr(), L.u32p))
+                          status=C.cast(stats["status"].data_ptr(), L.i32p))
+    if visited:  # the visited count and order: the search keeps the exact visited set
+        out.visited = C.cast(stats["visited"].data_ptr(), L.u32p)
+        out.history = C.cast(hist.data_ptr(), L.u32p)
+        out.history_cap = HIST
+        out.history_len = C.cast(stats["history_len"].data_ptr(), L.u32p)
     stream = torch.cuda.Stream()
     L.check(fn(dev._h, qt.data_ptr(), nq, C.byref(params), C.byref(out), stream.cuda_stream))
     torch.cuda.synchronize()
@@ -95,3 +97,26 @@ def test_noalloc_spilling_queries_reuse_slots(small_case, raven_lib):
     for _ in range(2):
         got = _run(raven_lib, L, raven_lib.raven_search_batch_device_noalloc, dev, qq, params)
         _same(got, want)
+
+
+def test_noalloc_without_visited_counts(small_case, raven_lib):
+    """Without the visited count and order the search keeps no visited tables
+    (pool membership decides new neighbours) and the fixed array holds only
+    the work counter and the ef table: 4,000 queries at ef=200 in one grid,
+    twice in a row, against the allocating search in the same mode and in the
+    exact-visited mode."""
+    from raven_b200 import _lib as L
+    from raven_b200.index import DeviceIndex
+
+    base, q, g = small_case
+    dev = DeviceIndex(g, base, sq4=True, adaptive=True)
+    qq = np.ascontiguousarray(np.tile(q, (10, 1)))
+    for params in (_params(L, ef=200), _params(L, ef=100, adaptive=1, gamma=2.0, min_ef=35, max_ef=120)):
+        exact = _run(raven_lib, L, raven_lib.raven_search_batch_device, dev, qq, params)
+        want = _run(raven_lib, L, raven_lib.raven_search_batch_device, dev, qq, params, visited=False)
+        for _ in range(2):
+            got = _run(raven_lib, L, raven_lib.raven_search_batch_device_noalloc, dev, qq, params, visited=False)
+            assert np.all(got["status"] == 0)
+            for key in ("ids", "dists", "counts", "ef_used"):
+                np.testing.assert_array_equal(got[key], want[key], err_msg=key)
+                np.testing.assert_array_equal(got[key], exact[key], err_msg=key)
