@@ -158,7 +158,15 @@ typedef struct {
  * unfilled slots id 0 / dist 0 (PyO3 batch_search padding, src/python.rs:344-349).
  * Any pointer but ids may be NULL. history (optional): nq*history_cap, the
  * visited nodes of each query in VisitedTracker order, with the full count in
- * history_len (entries beyond history_cap are not stored). */
+ * history_len (entries beyond history_cap are not stored).
+ *
+ * visited / history / history_len cost time: with any of them set, an SQ4/SQ8
+ * search keeps the exact visited set (a shared-memory table per query with
+ * global spill tables behind it). With all three NULL it decides new
+ * neighbours by pool membership instead, which accepts exactly the same
+ * candidates (a visited node outside the pool never beats the pool's worst
+ * entry), so every other output is identical; it needs no spill tables and
+ * runs faster. The f32 traversal always keeps the visited set. */
 typedef struct {
   uint32_t* ids;
   float* dists;
@@ -245,13 +253,13 @@ RAVEN_API void raven_limits(raven_limits_t* out);
 RAVEN_API int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bits);
 
 /* Small-batch path (no reference counterpart): a search of at most `max_nq`
- * queries runs one CTA of four warps per query, with the visited set in a
- * 2^14-slot shared-memory table, instead of the persistent one-warp-per-query
- * kernel; results are identical. RAVEN_SMALL_BATCH_AUTO (the default after
- * upload): as many queries as one wave of such CTAs holds (three per SM at dim
- * 128); 0 disables it (every batch uses the persistent kernel). Applies to
- * SQ4/SQ8 searches without rerank_f16 through raven_search_batch and
- * raven_search_batch_device. */
+ * queries runs one CTA of four warps per query (with the visited set, when
+ * requested, in a 2^14-slot shared-memory table) instead of the persistent
+ * one-warp-per-query kernel; results are identical. RAVEN_SMALL_BATCH_AUTO
+ * (the default after upload): as many queries as one wave of such CTAs holds,
+ * at most four per SM (592 queries on 148 SMs); 0 disables it (every batch
+ * uses the persistent kernel). Applies to SQ4/SQ8 searches without
+ * rerank_f16 through raven_search_batch and raven_search_batch_device. */
 #define RAVEN_SMALL_BATCH_AUTO (~(uint64_t)0)
 RAVEN_API int raven_index_set_small_batch(raven_index* ix, uint64_t max_nq);
 

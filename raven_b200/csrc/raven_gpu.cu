@@ -511,41 +511,42 @@ bool needs_visited(int quant, const raven_search_outputs* o) {
 }
 
 template <int QUANT, int CPL>
-cudaError_t launch_cta_t(const SearchArgs& a, uint32_t smem, uint64_t nq, cudaStream_t st) {
-  auto k = search_cta_kernel<QUANT, CPL>;
+cudaError_t launch_cta_t(const SearchArgs& a, bool vis, uint32_t smem, uint64_t nq, cudaStream_t st) {
+  auto k = vis ? search_cta_kernel<QUANT, CPL, true> : search_cta_kernel<QUANT, CPL, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k<<<(unsigned)nq, kCtaThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
 template <int QUANT, int CPL>
-cudaError_t occupancy_cta_t(uint32_t smem, int* per_sm) {
-  auto k = search_cta_kernel<QUANT, CPL>;
+cudaError_t occupancy_cta_t(bool vis, uint32_t smem, int* per_sm) {
+  auto k = vis ? search_cta_kernel<QUANT, CPL, true> : search_cta_kernel<QUANT, CPL, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k, kCtaThreads, smem);
 }
 template <int QUANT>
-cudaError_t occupancy_cta_cpl(int cpl, uint32_t smem, int* per_sm) {
+cudaError_t occupancy_cta_cpl(int cpl, bool vis, uint32_t smem, int* per_sm) {
   switch (cpl) {
-    case 1: return occupancy_cta_t<QUANT, 1>(smem, per_sm);
-    case 2: return occupancy_cta_t<QUANT, 2>(smem, per_sm);
-    case 4: return occupancy_cta_t<QUANT, 4>(smem, per_sm);
-    case 8: return occupancy_cta_t<QUANT, 8>(smem, per_sm);
+    case 1: return occupancy_cta_t<QUANT, 1>(vis, smem, per_sm);
+    case 2: return occupancy_cta_t<QUANT, 2>(vis, smem, per_sm);
+    case 4: return occupancy_cta_t<QUANT, 4>(vis, smem, per_sm);
+    case 8: return occupancy_cta_t<QUANT, 8>(vis, smem, per_sm);
   }
   return cudaErrorInvalidValue;
 }
 template <int QUANT>
-cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, uint32_t smem, uint64_t nq, cudaStream_t st) {
+cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, bool vis, uint32_t smem, uint64_t nq, cudaStream_t st) {
   switch (cpl) {
-    case 1: return launch_cta_t<QUANT, 1>(a, smem, nq, st);
-    case 2: return launch_cta_t<QUANT, 2>(a, smem, nq, st);
-    case 4: return launch_cta_t<QUANT, 4>(a, smem, nq, st);
-    case 8: return launch_cta_t<QUANT, 8>(a, smem, nq, st);
+    case 1: return launch_cta_t<QUANT, 1>(a, vis, smem, nq, st);
+    case 2: return launch_cta_t<QUANT, 2>(a, vis, smem, nq, st);
+    case 4: return launch_cta_t<QUANT, 4>(a, vis, smem, nq, st);
+    case 8: return launch_cta_t<QUANT, 8>(a, vis, smem, nq, st);
   }
   return cudaErrorInvalidValue;
 }
 
+constexpr int kCtaAutoPerSm = 4;  // small-batch kernel: default limit, resident CTAs per SM
 constexpr uint32_t kMaxEf = 256;
 constexpr uint32_t kMaxDimSq4 = 256;
 constexpr uint32_t kMaxDimSq8 = 128;
@@ -705,19 +706,29 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
   a.hist_len = o->history_len;
 }
 
-// Small batches: one CTA of four warps per query (search_cta.cuh), the visited
-// set in a 2^14-slot shared table; per-query global spill tables (2^13-slot
-// level A, level B 8x) stay allocated for exactness, touched only by a query
-// that fills the shared table. Same results as the batch kernel.
-int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p, const Plan& pl,
-                   const raven_search_outputs* o, cudaStream_t st) {
+// Shared-memory visited-table bits of the small-batch kernel (0: none).
+uint32_t cta_hash_bits(const raven_index* ix, bool vis) {
+  if (!vis) return 0;
   // the tuning hook can shrink the table (tests reach the spill levels this way)
   uint32_t hb = ix->hash_bits_override ? std::min<uint32_t>((uint32_t)ix->hash_bits_override, kCtaHashBits)
                                        : kCtaHashBits;
   while ((1u << hb) < ix->dim_pad) ++hb;
+  return hb;
+}
+
+// Small batches: one CTA of four warps per query (search_cta.cuh). With the
+// visited count or order requested, the visited set lives in a 2^14-slot
+// shared table, and per-query global spill tables (2^13-slot level A, level B
+// 8x) stay allocated for exactness, touched only by a query that fills the
+// shared table; otherwise pool membership decides and nothing is allocated
+// but the ef table. Same results as the batch kernel.
+int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p, const Plan& pl,
+                   const raven_search_outputs* o, cudaStream_t st) {
+  const bool vis = needs_visited(pl.quant, o);
+  const uint32_t hb = cta_hash_bits(ix, vis);
   const uint32_t kSpill = ix->spill_bits_override ? std::min<uint32_t>((uint32_t)ix->spill_bits_override, 13u) : 13u;
   const uint32_t smem = cta_smem_bytes(ix->dim_pad, ix->q_stride[pl.quant], pl.pool_cap, hb, ix->r_pad);
-  const size_t spill_bytes = (size_t)nq * (9ull << kSpill) * 4;
+  const size_t spill_bytes = vis ? (size_t)nq * (9ull << kSpill) * 4 : 0;
   const size_t table_bytes = pl.table.size() * 4;
   uint8_t* scratch = nullptr;
   CU(cudaMallocAsync((void**)&scratch, spill_bytes + ((table_bytes + 255) & ~(size_t)255) + 256, st));
@@ -731,13 +742,14 @@ int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_s
     a.hash_bits = hb;
     a.spill_bits = kSpill;
     a.ef_table = table;
-    a.spill = spill;
+    a.spill = vis ? spill : nullptr;
     a.n_slots = nq;
     a.queries = d_q;
     a.nq = nq;
     a.counter = nullptr;
     a.nav_only = 0;
-    e = pl.quant == 0 ? dispatch_cta_cpl<0>(pl.cpl, a, smem, nq, st) : dispatch_cta_cpl<1>(pl.cpl, a, smem, nq, st);
+    e = pl.quant == 0 ? dispatch_cta_cpl<0>(pl.cpl, a, vis, smem, nq, st)
+                      : dispatch_cta_cpl<1>(pl.cpl, a, vis, smem, nq, st);
   }
   cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("small-batch search launch: ") + cudaGetErrorString(e));
@@ -764,9 +776,14 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
     uint64_t lim = ix->small_batch_max;
     if (lim == ~0ull) {  // as many queries as one wave of CTAs holds
       int per_sm = 0;
-      const uint32_t smem = cta_smem_bytes(ix->dim_pad, ix->q_stride[pl.quant], pl.pool_cap, kCtaHashBits, ix->r_pad);
-      CU(pl.quant == 0 ? occupancy_cta_cpl<0>(pl.cpl, smem, &per_sm) : occupancy_cta_cpl<1>(pl.cpl, smem, &per_sm));
-      lim = (uint64_t)std::max(per_sm, 0) * (uint64_t)ix->num_sms;
+      const bool vis = needs_visited(pl.quant, o);
+      const uint32_t smem =
+          cta_smem_bytes(ix->dim_pad, ix->q_stride[pl.quant], pl.pool_cap, vis ? kCtaHashBits : 0u, ix->r_pad);
+      CU(pl.quant == 0 ? occupancy_cta_cpl<0>(pl.cpl, vis, smem, &per_sm)
+                       : occupancy_cta_cpl<1>(pl.cpl, vis, smem, &per_sm));
+      // measured on a 1M-node graph (ef 50 and 140): the persistent kernel
+      // takes over between 3 and 6 resident CTAs per SM
+      lim = (uint64_t)std::min(std::max(per_sm, 0), kCtaAutoPerSm) * (uint64_t)ix->num_sms;
     }
     if (nq <= lim) return run_search_cta(ix, d_q, nq, p, pl, o, st);
   }

@@ -3,10 +3,13 @@
 // A batch smaller than the GPU leaves most SMs idle under the persistent
 // one-warp-per-query kernel, and each query's latency is one warp's chain of
 // dependent expansions. Here each query gets a whole CTA:
-//   * the visited set lives in a shared-memory table of 2^14 slots (64 KB,
-//     over 14,000 visits; three CTAs fit an SM), so a query does not reach the
-//     global spill levels in practice (they remain, for exactness, behind the
-//     same capacity checks as in the batch kernel);
+//   * VIS true (visited count or order requested): the visited set lives in a
+//     shared-memory table of 2^14 slots (64 KB, over 14,000 visits; three CTAs
+//     fit an SM), so a query does not reach the global spill levels in
+//     practice (they remain, for exactness, behind the same capacity checks
+//     as in the batch kernel). VIS false: no visited set; pool membership
+//     decides new neighbours, with the same results (the argument is in
+//     search_kernel.cuh), and a CTA needs only its pool and staging rows;
 //   * the four warps share each expansion's work: every warp gathers the
 //     codes of eight of the row's neighbours and computes their distances,
 //     while warp 0 also runs the visited set and then the pool merge; the
@@ -36,16 +39,16 @@ struct CtaSmem {
   uint32_t* cand_d;   // 2 x 32: beam distances of a segment's neighbours (by segment parity)
   float* nd;          // 32: navigation / rerank distances
   uint32_t* rowbuf;   // 2 x r_pad: adjacency rows prefetched by cp.async
-  uint32_t* crow;     // r_pad: the row being expanded, for every warp
+  uint32_t* crow;     // 2 x r_pad: the row being expanded, for every warp (by expansion parity)
   uint32_t* ctl;      // 16 control words shared by the warps
   uint32_t* ht;       // cta_table_bytes: visited table (1 << hash_bits); row staging outside the beam
 };
 
 // The last region holds the visited table during the beam and the row staging
 // of cta_rows_dist (kCtaWarps x kCtaRowsPerWarp rows) outside it: it is sized
-// for the larger of the two.
+// for the larger of the two (hash_bits 0: no visited table).
 __host__ __device__ inline uint32_t cta_table_bytes(uint32_t dim_pad, uint32_t hash_bits) {
-  const uint32_t table = align16((1u << hash_bits) * 4);
+  const uint32_t table = hash_bits ? align16((1u << hash_bits) * 4) : 0u;
   const uint32_t stage = (uint32_t)(kCtaWarps * kCtaRowsPerWarp) * dim_pad * 4;
   return table > stage ? table : stage;
 }
@@ -53,7 +56,7 @@ __host__ __device__ inline uint32_t cta_table_bytes(uint32_t dim_pad, uint32_t h
 __host__ __device__ inline uint32_t cta_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pool_cap,
                                                    uint32_t hash_bits, uint32_t r_pad) {
   return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(pool_cap * 4) + 128 + 256 + 128 +
-         2 * r_pad * 4 + r_pad * 4 + 64 + cta_table_bytes(dim_pad, hash_bits);
+         2 * r_pad * 4 + 2 * r_pad * 4 + 64 + cta_table_bytes(dim_pad, hash_bits);
 }
 
 __device__ inline CtaSmem cta_carve(uint8_t* base, const SearchArgs& a) {
@@ -76,7 +79,7 @@ __device__ inline CtaSmem cta_carve(uint8_t* base, const SearchArgs& a) {
   s.rowbuf = (uint32_t*)(base + o);
   o += 2 * a.r_pad * 4;
   s.crow = (uint32_t*)(base + o);
-  o += a.r_pad * 4;
+  o += 2 * a.r_pad * 4;
   s.ctl = (uint32_t*)(base + o);
   o += 64;
   s.ht = (uint32_t*)(base + o);
@@ -193,7 +196,7 @@ __device__ inline bool cta_nav_descend(const SearchArgs& a, const CtaSmem& s, in
 // QUANT 0 (SQ4) or 1 (SQ8); f16 reranks and the f32 traversal use the batch
 // kernel. Level-A/B spill tables of query q start at a.spill + q * (9 <<
 // spill_bits) (only touched by a query that fills the shared table).
-template <int QUANT, int CPL>
+template <int QUANT, int CPL, bool VIS>
 __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const SearchArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -290,10 +293,12 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
             b < a.dim ? (uint8_t)quantize(s.qf[lane_major_pos(b, a.vec_c)], a.q_inv[b], a.q_neg[b], a.levels)
                       : (uint8_t)0;
     }
-    // clear the visited table (the descent's staging rows are done)
-    for (uint32_t i = tid * 4; i < H; i += 4 * kCtaThreads)
-      *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-    __syncthreads();
+    if (VIS) {
+      // clear the visited table (the descent's staging rows are done)
+      for (uint32_t i = tid * 4; i < H; i += 4 * kCtaThreads)
+        *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
+    }
+    __syncthreads();  // the query code (and the table) are written before any warp reads them
     QChunk<QUANT> qc;
     qc.load(s.qcode, sub);
 
@@ -306,9 +311,11 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
     const uint32_t RL = a.r_pad >> 5;
     if (w == 0) {
       // 4. entry
-      if (lane == 0) shared_insert2(s.ht, a.hash_bits - 2, entry);
-      tcount = 1;
-      if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
+      if (VIS) {
+        if (lane == 0) shared_insert2(s.ht, a.hash_bits - 2, entry);
+        tcount = 1;
+        if (a.history && lane == 0 && a.hist_cap > 0) a.history[qi * a.hist_cap] = entry;
+      }
       vcount = 1;
       int pd = 0;
       if (grp == 0) {
@@ -341,10 +348,14 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           ++expansions;
           cp_async_wait_all();
           __syncwarp();
+          // the row goes to crow's half for this expansion's parity: a warp
+          // still reading the previous row (it has no barrier left to pass
+          // when that row ended early) reads the other half
+          uint32_t* cw = s.crow + (it & 1) * a.r_pad;
           if (node == pref_node) {
-            for (uint32_t i = lane; i < a.r_pad; i += 32) s.crow[i] = s.rowbuf[pbuf * a.r_pad + i];
+            for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = s.rowbuf[pbuf * a.r_pad + i];
           } else {
-            for (uint32_t i = lane; i < a.r_pad; i += 32) s.crow[i] = __ldg(a.adj + (size_t)node * a.r_pad + i);
+            for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = __ldg(a.adj + (size_t)node * a.r_pad + i);
           }
           __syncwarp();  // both buffers read before new copies are issued
           nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
@@ -360,13 +371,17 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
       }
       __syncthreads();
       if (s.ctl[it & 1] == 0) break;
+      const uint32_t* cr = s.crow + (it & 1) * a.r_pad;
       ++it;
 
+      uint32_t row[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) row[r] = (uint32_t)r < RL ? cr[32 * r + lane] : kSent;
       bool early = false;
       bool overflow = false;
       int first_insert = 0x7fffffff;
       for (uint32_t seg = 0; seg < RL; ++seg) {
-        const uint32_t id = s.crow[seg * 32 + lane];
+        const uint32_t id = seg == 0 ? row[0] : seg == 1 ? row[1] : seg == 2 ? row[2] : row[3];
         const uint32_t sm = __ballot_sync(kFull, id == kSent);
         const int deg = sm ? __ffs(sm) - 1 : 32;
         if (deg == 0) break;  // the row ended at the previous segment
@@ -387,8 +402,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
         }
         // warp 0: the visited set, in adjacency order (the batch kernel's levels)
         bool is_new = false;
-        if (w == 0) {
-          const bool valid = lane < deg;
+        const bool valid = lane < deg;
+        if (VIS && w == 0) {
           if (level == 0 && tcount + 32 > h_limit) {
             if (spill == nullptr) {
               overflow = true;
@@ -456,30 +471,39 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           if (sub == 0 && idxr[r] >= 0) cd[idxr[r]] = (uint32_t)pdist;
         }
         __syncthreads();
-        if (s.ctl[2 + par] != 0) {
+        if (VIS && s.ctl[2 + par] != 0) {
           overflow = true;
           break;
         }
         if (w == 0) {
           // warp 0: LinearPool insert of the new neighbours, batched (as in the batch kernel)
-          const uint32_t my_d = is_new ? cd[lane] : 0xffffffffu;
+          const bool cand = VIS ? is_new : valid;
+          const uint32_t my_d = cand ? cd[lane] : 0xffffffffu;
           const bool full = sz == (int)ef;
           const uint32_t worst = full ? s.pool_d[sz - 1] : 0xffffffffu;
-          const bool acc = is_new && (!full || my_d < worst);
+          bool acc = cand && (!full || my_d < worst);
+          int lo = 0;  // # pool entries <= my_d (ties: pool first)
+          if (acc) {
+            int hi = sz;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (s.pool_d[mid] <= my_d) lo = mid + 1;
+              else hi = mid;
+            }
+            // without the visited set: a neighbour already in the pool sits
+            // in the run of equal distances ending at lo - 1
+            if (!VIS)
+              for (int j = lo - 1; j >= 0 && s.pool_d[j] == my_d; --j)
+                if ((s.pool_id[j] & ~kChecked) == id) {
+                  acc = false;
+                  break;
+                }
+          }
           const uint32_t am = __ballot_sync(kFull, acc);
           const int na = __popc(am);
           __syncwarp();
           if (na > 0) {
-            int cpos = 0x7fffffff;
-            if (acc) {
-              int lo = 0, hi = sz;
-              while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (s.pool_d[mid] <= my_d) lo = mid + 1;
-                else hi = mid;
-              }
-              cpos = lo;
-            }
+            int cpos = acc ? lo : 0x7fffffff;
             const int start = (int)__reduce_min_sync(kFull, (unsigned)cpos);
             if (start <= min(nxt, first_insert)) {
               const uint32_t dmin = __reduce_min_sync(kFull, acc ? my_d : 0xffffffffu);
@@ -594,12 +618,12 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
   }
   if (lane == 0) {
     if (a.counts) a.counts[qi] = (uint32_t)kout;
-    if (a.visited) a.visited[qi] = vcount;
+    if (VIS && a.visited) a.visited[qi] = vcount;
     if (a.ef_used) a.ef_used[qi] = ef;
     if (a.status) a.status[qi] = status;
     if (a.n_nav) a.n_nav[qi] = n_nav;
     if (a.expansions) a.expansions[qi] = expansions;
-    if (a.hist_len) a.hist_len[qi] = vcount;
+    if (VIS && a.hist_len) a.hist_len[qi] = vcount;
   }
 }
 

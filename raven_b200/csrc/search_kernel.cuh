@@ -55,6 +55,7 @@ constexpr uint32_t kGidBit = 0x80000000u;  // nav handle: global id (node withou
 constexpr uint32_t kEmpty = 0xffffffffu;
 constexpr int kWarpsPerBlock = 4;
 constexpr int kMinBlocksPerSm = 6;  // 80 registers/thread: the measured best residency trade-off
+constexpr int kMinBlocksPerSmPool = 7;  // without a visited set: 72 registers, 7 blocks (measured best of 6/7/8)
 constexpr uint32_t kNavStepLimit = 1u << 16;
 
 struct SearchArgs {
@@ -684,7 +685,8 @@ struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
 // POOLMAX: 64 for pools of at most 64 entries (layout and merge bounds fixed
 // at compile time), 0 for a run-time capacity (a.pool_cap).
 template <int QUANT, int CPL, int POOLMAX, bool VIS>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_kernel(const SearchArgs a) {
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : kMinBlocksPerSmPool)
+    search_kernel(const SearchArgs a) {
   static_assert(VIS || QUANT != 2, "the f32 beam scores new neighbours only: it needs the visited set");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
@@ -805,8 +807,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, kMinBlocksPerSm) search_k
       if (VIS) {
         // clear the visited table (the staging rows of the descent are done)
         for (uint32_t i = lane * 4; i < H; i += 128) *(uint4*)(s.ht + i) = make_uint4(kEmpty, kEmpty, kEmpty, kEmpty);
-        __syncwarp();
       }
+      __syncwarp();  // the query code (and the table) are written before any lane reads them
       QChunk<QUANT> qc;
       qc.load(s.qcode, sub);
 

@@ -202,7 +202,7 @@ class DeviceIndex:
 
     def set_small_batch(self, max_nq: int) -> None:
         """Batches of at most `max_nq` queries run one CTA per query (0: never;
-        SMALL_BATCH_AUTO, the default: one wave of CTAs)."""
+        SMALL_BATCH_AUTO, the default: one wave of CTAs, at most four per SM)."""
         L.check(L.load().raven_index_set_small_batch(self._h, max_nq))
 
     def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True,
