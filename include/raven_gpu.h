@@ -263,6 +263,16 @@ RAVEN_API int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t
 #define RAVEN_SMALL_BATCH_AUTO (~(uint64_t)0)
 RAVEN_API int raven_index_set_small_batch(raven_index* ix, uint64_t max_nq);
 
+/* Neighbour codes beside each row (no reference counterpart): for every
+ * uploaded quantiser, n x R_pad x code-stride bytes in which node i's slot j
+ * holds the code of its j-th neighbour (2 GB for 1M nodes, R_pad 32, SQ4 at
+ * dim 128). A search without visited counts then reads an expansion's codes
+ * as one contiguous piece, prefetched with the row, instead of gathering them
+ * from R scattered nodes. Built at upload when they fit in half of the free
+ * device memory; enable = 0 frees them, 1 (re)builds them. Results are
+ * identical either way. */
+RAVEN_API int raven_index_set_fat_rows(raven_index* ix, int32_t enable);
+
 RAVEN_API const char* raven_last_error(void);
 RAVEN_API const char* raven_version(void);
 

@@ -141,6 +141,7 @@ SIGNATURES = {
     "raven_limits": (None, [C.POINTER(Limits)]),
     "raven_index_set_tuning": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32]),
     "raven_index_set_small_batch": (C.c_int, [C.c_void_p, C.c_uint64]),
+    "raven_index_set_fat_rows": (C.c_int, [C.c_void_p, C.c_int32]),
     "raven_last_error": (C.c_char_p, []),
     "raven_version": (C.c_char_p, []),
 }

@@ -47,6 +47,9 @@ struct raven_index {
   bool has_q[2] = {false, false};
   uint32_t q_stride[2] = {0, 0};
   uint8_t* d_codes[2] = {nullptr, nullptr};
+  // neighbour codes beside each row: node i's slot j holds the code of
+  // adj[i][j] (zeros past the degree), n x r_pad x q_stride bytes, or null
+  uint8_t* d_fat[2] = {nullptr, nullptr};
   float* d_qparams[2] = {nullptr, nullptr};  // 5*dim
   std::vector<float> h_qparams[2];
   bool has_nav = false;
@@ -97,6 +100,26 @@ uint32_t next_pow2(uint32_t x) {
 // and SQ8Params::encode_all (src/quant/sq8.rs:100-111). One thread per output
 // 4-byte word; padding bytes are zero.
 // ---------------------------------------------------------------------------
+
+// Neighbour codes beside each row: fat[i][j] = codes[adj[i][j]], zeros for
+// SENTINEL slots. One warp per row, 16-byte pieces (stride is a multiple of
+// 16). Grid-stride over rows.
+__global__ void fat_rows_kernel(const uint32_t* __restrict__ adj, const uint8_t* __restrict__ codes, uint64_t n,
+                                uint32_t r_pad, uint32_t stride, uint8_t* __restrict__ fat) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x >> 5);
+  const uint32_t pieces = stride >> 4;  // per code
+  const uint32_t total = r_pad * pieces;
+  for (uint64_t row = (uint64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < n; row += warps) {
+    uint4* dst = (uint4*)(fat + row * r_pad * stride);
+    for (uint32_t t = lane; t < total; t += 32) {
+      const uint32_t j = t / pieces, pc = t - j * pieces;
+      const uint32_t id = adj[row * r_pad + j];
+      dst[t] = id == 0xFFFFFFFFu ? make_uint4(0, 0, 0, 0) : ((const uint4*)(codes + (size_t)id * stride))[pc];
+    }
+  }
+}
+
 __global__ void encode_kernel(const float* __restrict__ v, uint64_t n, uint32_t dim, const float* __restrict__ inv,
                               const float* __restrict__ neg, float levels, int sq4, uint32_t stride,
                               uint32_t* __restrict__ out) {
@@ -690,6 +713,8 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
   a.k = p->k;
   a.rr = std::max<uint32_t>(p->rerank_factor, 1);
   a.hash_bits = pl.hash_bits;
+  // neighbour codes beside the rows (read by the small-batch search without a visited set)
+  a.fat = f32 ? nullptr : ix->d_fat[pl.quant];
   a.spill_bits = pl.spill_bits;
   a.smem_per_warp = pl.smem_warp;
   a.f32_stage_rows = pl.f32_stage_rows;
@@ -836,6 +861,29 @@ int dev_alloc_copy(T** dst, const T* src, size_t count) {
   return RAVEN_OK;
 }
 
+// Builds (or frees) the neighbour codes beside each row for quantiser q.
+// Skipped, not failed, when they would take more than half of the free device
+// memory: the search then gathers the codes from the code array instead.
+int set_fat_rows(raven_index* ix, int q, bool enable) {
+  cudaFree(ix->d_fat[q]);
+  ix->d_fat[q] = nullptr;
+  if (!enable || !ix->has_q[q]) return RAVEN_OK;
+  const size_t bytes = (size_t)ix->n * ix->r_pad * ix->q_stride[q];
+  size_t free_b = 0, total_b = 0;
+  CU(cudaMemGetInfo(&free_b, &total_b));
+  if (bytes > free_b / 2) return RAVEN_OK;
+  if (cudaMalloc((void**)&ix->d_fat[q], bytes) != cudaSuccess) {
+    cudaGetLastError();
+    ix->d_fat[q] = nullptr;
+    return RAVEN_OK;
+  }
+  fat_rows_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(ix->d_adj, ix->d_codes[q], ix->n, ix->r_pad,
+                                                          ix->q_stride[q], ix->d_fat[q]);
+  CU(cudaGetLastError());
+  CU(cudaStreamSynchronize(ix->stream));
+  return RAVEN_OK;
+}
+
 void free_index(raven_index* ix) {
   if (!ix) return;
   cudaSetDevice(ix->device);
@@ -844,6 +892,7 @@ void free_index(raven_index* ix) {
   cudaFree(ix->d_adj);
   for (int q = 0; q < 2; ++q) {
     cudaFree(ix->d_codes[q]);
+    cudaFree(ix->d_fat[q]);
     cudaFree(ix->d_qparams[q]);
   }
   cudaFree(ix->d_nav_vec);
@@ -1065,6 +1114,7 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
                                                           q == 0, stride, (uint32_t*)ix->d_codes[q]);
     if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "encode launch failed"));
     ix->has_q[q] = true;
+    if ((rc = set_fat_rows(ix, q, true))) return bail2(rc);
   }
   // navigation layers: every node with an upper list gets a slot; its edges
   // are stored per level at a fixed stride (stride_levels x k, kSent padded)
@@ -1490,6 +1540,18 @@ int raven_index_set_tuning(raven_index* ix, int32_t hash_bits, int32_t spill_bit
   if (spill_bits && (spill_bits < 10 || spill_bits > 20)) return fail(RAVEN_EINVAL, "spill_bits must be in 10..20");
   ix->hash_bits_override = hash_bits;
   ix->spill_bits_override = spill_bits;
+  return RAVEN_OK;
+}
+
+// Neighbour codes beside each row (no reference counterpart): built by
+// default at upload; disabling frees them (the search gathers codes instead).
+int raven_index_set_fat_rows(raven_index* ix, int32_t enable) {
+  if (!ix) return fail(RAVEN_EINVAL, "null index");
+  CU(cudaSetDevice(ix->device));
+  for (int q = 0; q < 2; ++q) {
+    const int rc = set_fat_rows(ix, q, enable != 0);
+    if (rc) return rc;
+  }
   return RAVEN_OK;
 }
 

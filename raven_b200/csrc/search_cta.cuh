@@ -41,6 +41,7 @@ struct CtaSmem {
   uint32_t* rowbuf;   // 2 x r_pad: adjacency rows prefetched by cp.async
   uint32_t* crow;     // 2 x r_pad: the row being expanded, for every warp (by expansion parity)
   uint32_t* ctl;      // 16 control words shared by the warps
+  uint8_t* fbuf;      // 2 x 32 x code_stride: first 32 neighbour codes of a predicted expansion
   uint32_t* ht;       // cta_table_bytes: visited table (1 << hash_bits); row staging outside the beam
 };
 
@@ -56,7 +57,7 @@ __host__ __device__ inline uint32_t cta_table_bytes(uint32_t dim_pad, uint32_t h
 __host__ __device__ inline uint32_t cta_smem_bytes(uint32_t dim_pad, uint32_t code_stride, uint32_t pool_cap,
                                                    uint32_t hash_bits, uint32_t r_pad) {
   return align16(dim_pad * 4) + align16(code_stride) + 2 * align16(pool_cap * 4) + 128 + 256 + 128 +
-         2 * r_pad * 4 + 2 * r_pad * 4 + 64 + cta_table_bytes(dim_pad, hash_bits);
+         2 * r_pad * 4 + 2 * r_pad * 4 + 64 + 64 * code_stride + cta_table_bytes(dim_pad, hash_bits);
 }
 
 __device__ inline CtaSmem cta_carve(uint8_t* base, const SearchArgs& a) {
@@ -82,6 +83,8 @@ __device__ inline CtaSmem cta_carve(uint8_t* base, const SearchArgs& a) {
   o += 2 * a.r_pad * 4;
   s.ctl = (uint32_t*)(base + o);
   o += 64;
+  s.fbuf = base + o;
+  o += 64 * a.code_stride;
   s.ht = (uint32_t*)(base + o);
   return s;
 }
@@ -308,7 +311,15 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
     int cursor = 0;
     uint32_t pref_node = kSent;
     int pbuf = 0;
+    int eb = 1;  // buffer of an early prediction during this expansion
     const uint32_t RL = a.r_pad >> 5;
+    // Without the visited set, warp 0 prefetches the first 32 neighbour codes
+    // of each predicted expansion (stored beside the rows) with its row, into
+    // one of two buffers; the expansion that finds its codes there reads them
+    // instead of gathering (ctl[8 + parity]: buffer + 1, 0 = gather), and new
+    // prefetches go to the other buffer until every warp has read them.
+    const bool use_fat = !VIS && a.fat != nullptr;
+    const uint32_t fb_bytes = 32u * a.code_stride;
     if (w == 0) {
       // 4. entry
       if (VIS) {
@@ -352,17 +363,22 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           // still reading the previous row (it has no barrier left to pass
           // when that row ended early) reads the other half
           uint32_t* cw = s.crow + (it & 1) * a.r_pad;
+          const int cur = (use_fat && node == pref_node) ? pbuf : -1;
           if (node == pref_node) {
             for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = s.rowbuf[pbuf * a.r_pad + i];
           } else {
             for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = __ldg(a.adj + (size_t)node * a.r_pad + i);
           }
+          if (lane == 0) s.ctl[8 + (it & 1)] = (uint32_t)(cur + 1);
           __syncwarp();  // both buffers read before new copies are issued
           nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
+          const int nb = cur == 0 ? 1 : 0;  // the next in pool order; an early prediction takes the other
+          eb = 1 - nb;
           if (nxt < sz) {
             pref_node = s.pool_id[nxt] & ~kChecked;
-            prefetch_row(a.adj, a.r_pad, s.rowbuf, pref_node, lane);
-            pbuf = 0;
+            if (use_fat) prefetch_fat(a.fat, a.r_pad, a.code_stride, s.fbuf + nb * fb_bytes, pref_node, lane, 32);
+            prefetch_row(a.adj, a.r_pad, s.rowbuf + nb * a.r_pad, pref_node, lane);
+            pbuf = nb;
           } else {
             pref_node = kSent;
           }
@@ -372,6 +388,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
       __syncthreads();
       if (s.ctl[it & 1] == 0) break;
       const uint32_t* cr = s.crow + (it & 1) * a.r_pad;
+      const uint32_t fsel = use_fat ? s.ctl[8 + (it & 1)] : 0u;  // prefetched codes: buffer + 1, or 0
       ++it;
 
       uint32_t row[4];
@@ -398,7 +415,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           idxr[r] = (loc < 8 && idx < deg) ? idx : -1;
           const uint32_t cid = __shfl_sync(kFull, id, idx & 31);
           const uint32_t c = idxr[r] >= 0 ? cid : 0u;  // address always in range
-          data[r] = __ldg((const uint4*)(a.codes + (size_t)c * a.code_stride) + sub);
+          if (seg == 0 && fsel != 0)  // the prefetched copy (slot idx & 31 is always in the buffer)
+            data[r] = *((const uint4*)(s.fbuf + (fsel - 1) * fb_bytes + (size_t)(idx & 31) * a.code_stride) + sub);
+          else
+            data[r] = __ldg((const uint4*)(a.codes + (size_t)c * a.code_stride) + sub);
         }
         // warp 0: the visited set, in adjacency order (the batch kernel's levels)
         bool is_new = false;
@@ -512,8 +532,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
                 cp_async_wait_all();
                 __syncwarp();
               }
-              prefetch_row(a.adj, a.r_pad, s.rowbuf + a.r_pad, pref_node, lane);
-              pbuf = 1;
+              if (use_fat) prefetch_fat(a.fat, a.r_pad, a.code_stride, s.fbuf + eb * fb_bytes, pref_node, lane, 32);
+              prefetch_row(a.adj, a.r_pad, s.rowbuf + eb * a.r_pad, pref_node, lane);
+              pbuf = eb;
               early = true;
             }
             int crank = 0;
@@ -564,6 +585,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
         if (cursor > sz) cursor = sz;
       }
     }
+    if (w == 0) cp_async_wait_all();  // nothing left in flight
     // publish the pool size for the rerank
     if (w == 0 && lane == 0) s.ctl[6] = (uint32_t)sz;
     __syncthreads();

@@ -114,6 +114,9 @@ struct SearchArgs {
   unsigned long long* counter;
   int nav_only;  // 1: only run the descent; write entry to ids[q], distance to dists[q]
   uint32_t f32_stage_rows;  // QUANT 2: rows staged per round for the beam's f32 distances
+  // neighbour codes beside each row (n x r_pad x code_stride), or null; read
+  // by the small-batch kernel without a visited set
+  const uint8_t* __restrict__ fat;
 };
 
 // Per-warp shared-memory carve-up (every piece 16-byte aligned).
@@ -188,6 +191,13 @@ __device__ inline void cp_async4(void* smem, const void* gmem) {
 __device__ inline void prefetch_row(const uint32_t* adj, uint32_t r_pad, uint32_t* buf, uint32_t node, int lane) {
   if ((uint32_t)lane < (r_pad >> 2)) cp_async16(buf + 4 * lane, adj + (size_t)node * r_pad + 4 * lane);
   asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+// The first 32 neighbour codes of `node` (32 x stride bytes) into shared
+// memory, copied by the `nthreads` threads t = 0.. of the caller.
+__device__ inline void prefetch_fat(const uint8_t* fat, uint32_t r_pad, uint32_t stride, uint8_t* buf, uint32_t node,
+                                    int t, int nthreads) {
+  const uint8_t* src = fat + (size_t)node * r_pad * stride;
+  for (uint32_t i = (uint32_t)t; i < 2u * stride; i += (uint32_t)nthreads) cp_async16(buf + 16 * i, src + 16 * i);
 }
 __device__ inline void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");

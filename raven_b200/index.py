@@ -205,6 +205,11 @@ class DeviceIndex:
         SMALL_BATCH_AUTO, the default: one wave of CTAs, at most four per SM)."""
         L.check(L.load().raven_index_set_small_batch(self._h, max_nq))
 
+    def set_fat_rows(self, enable: bool) -> None:
+        """Neighbour codes stored beside each row (default: built at upload when
+        they fit); False frees them and the search gathers codes instead."""
+        L.check(L.load().raven_index_set_fat_rows(self._h, int(bool(enable))))
+
     def search(self, queries, params: L.SearchParams, history_cap: int = 0, stats: bool = True,
                visited: Optional[bool] = None) -> dict:
         """Host-buffer batch search (raven_search_batch). Returns a dict of arrays.
