@@ -504,12 +504,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           bool acc = cand && (!full || my_d < worst);
           int lo = 0;  // # pool entries <= my_d (ties: pool first)
           if (acc) {
-            int hi = sz;
-            while (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              if (s.pool_d[mid] <= my_d) lo = mid + 1;
-              else hi = mid;
-            }
+            lo = pool_upper_bound(s.pool_d, sz, my_d);
             // without the visited set: a neighbour already in the pool sits
             // in the run of equal distances ending at lo - 1
             if (!VIS)
@@ -537,11 +532,19 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
               pbuf = eb;
               early = true;
             }
+            // rank among the accepted by (distance, lane), from the row's
+            // distances in shared memory: 32 independent compares instead of
+            // a chain of shuffles (an accepted lane's my_d is cd[lane])
             int crank = 0;
-            for (uint32_t m = am; m; m &= m - 1) {
-              const int jl = __ffs(m) - 1;
-              const uint32_t dj = __shfl_sync(kFull, my_d, jl);
-              crank += (dj < my_d) | ((dj == my_d) & (jl < lane));
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const uint4 q4 = *(const uint4*)(cd + 4 * j4);
+              const uint32_t dq[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int jl = 4 * j4 + u;
+                crank += (int)((am >> jl) & 1u) & ((dq[u] < my_d) | ((dq[u] == my_d) & (jl < lane)));
+              }
             }
             if (acc) cpos += crank;
             const int nsz = min(sz + na, (int)ef);

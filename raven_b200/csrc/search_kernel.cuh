@@ -606,6 +606,20 @@ __device__ inline bool spill_insert_warp(uint32_t* t, uint32_t bits, uint32_t id
   return is_new;
 }
 
+// Number of entries <= d in the sorted pool prefix [0, sz), for a candidate
+// that the pool accepts (so the answer is < 256 at the engine's pool limit of
+// 256): eight fixed steps, each one shared read and a select, instead of a
+// divergent loop.
+__device__ inline int pool_upper_bound(const uint32_t* pool_d, int sz, uint32_t d) {
+  int pos = 0;
+#pragma unroll
+  for (int step = 128; step > 0; step >>= 1) {
+    const int p = pos + step;
+    if (p <= sz && pool_d[p - 1] <= d) pos = p;
+  }
+  return pos;
+}
+
 __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, int lane) {
   for (int base = from & ~31; base < sz; base += 32) {
     const int p = base + lane;
@@ -1009,12 +1023,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
           bool acc = (VIS ? is_new : valid) && (!full || my_d < worst);
           int slot_lo = 0;  // without the visited set: # pool entries <= my_d
           if (!VIS && acc) {
-            int lo = 0, hi = sz;
-            while (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              if (s.pool_d[mid] <= my_d) lo = mid + 1;
-              else hi = mid;
-            }
+            const int lo = pool_upper_bound(s.pool_d, sz, my_d);
             slot_lo = lo;
             // already in the pool: an equal id sits in the run of equal
             // distances ending at lo - 1
@@ -1032,13 +1041,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
             int cpos = 0x7fffffff;
             if (acc && !VIS) cpos = slot_lo;
             if (acc && VIS) {
-              int lo = 0, hi = sz;  // # pool entries <= my_d (ties: pool first)
-              while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (s.pool_d[mid] <= my_d) lo = mid + 1;
-                else hi = mid;
-              }
-              cpos = lo;
+              cpos = pool_upper_bound(s.pool_d, sz, my_d);  // ties: pool first
             }
             const int start = (int)__reduce_min_sync(kFull, (unsigned)cpos);
             if (start <= min(nxt, first_insert)) {
