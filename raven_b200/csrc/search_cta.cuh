@@ -359,18 +359,16 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           ++expansions;
           cp_async_wait_all();
           __syncwarp();
-          // the row goes to crow's half for this expansion's parity: a warp
-          // still reading the previous row (it has no barrier left to pass
-          // when that row ended early) reads the other half
-          uint32_t* cw = s.crow + (it & 1) * a.r_pad;
-          const int cur = (use_fat && node == pref_node) ? pbuf : -1;
-          if (node == pref_node) {
-            for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = s.rowbuf[pbuf * a.r_pad + i];
-          } else {
+          // a predicted row (and its codes) is read where it was prefetched;
+          // otherwise warp 0 copies the row to crow's half for this
+          // expansion's parity
+          const int cur = node == pref_node ? pbuf : -1;
+          if (cur < 0) {
+            uint32_t* cw = s.crow + (it & 1) * a.r_pad;
             for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = __ldg(a.adj + (size_t)node * a.r_pad + i);
           }
           if (lane == 0) s.ctl[8 + (it & 1)] = (uint32_t)(cur + 1);
-          __syncwarp();  // both buffers read before new copies are issued
+          __syncwarp();  // the pop mark and the row copy are visible to every lane
           nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
           const int nb = cur == 0 ? 1 : 0;  // the next in pool order; an early prediction takes the other
           eb = 1 - nb;
@@ -387,8 +385,11 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
       }
       __syncthreads();
       if (s.ctl[it & 1] == 0) break;
-      const uint32_t* cr = s.crow + (it & 1) * a.r_pad;
-      const uint32_t fsel = use_fat ? s.ctl[8 + (it & 1)] : 0u;  // prefetched codes: buffer + 1, or 0
+      // the row: prefetch buffer + 1, or 0 for crow; the codes come from the
+      // same buffer when they were prefetched with it
+      const uint32_t rsel = s.ctl[8 + (it & 1)];
+      const uint32_t* cr = rsel ? s.rowbuf + (rsel - 1) * a.r_pad : s.crow + (it & 1) * a.r_pad;
+      const uint32_t fsel = use_fat ? rsel : 0u;
       ++it;
 
       uint32_t row[4];
@@ -401,7 +402,13 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
         const uint32_t id = seg == 0 ? row[0] : seg == 1 ? row[1] : seg == 2 ? row[2] : row[3];
         const uint32_t sm = __ballot_sync(kFull, id == kSent);
         const int deg = sm ? __ffs(sm) - 1 : 32;
-        if (deg == 0) break;  // the row ended at the previous segment
+        if (deg == 0) {
+          // the row ended at the previous segment; an empty row still takes
+          // one barrier, so that every warp has read it before warp 0 issues
+          // the next prefetch into its buffer
+          if (seg == 0) __syncthreads();
+          break;
+        }
         const uint32_t par = segs_done & 1;
         uint32_t* cd = s.cand_d + 32 * par;
         ++segs_done;
