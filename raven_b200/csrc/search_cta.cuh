@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
     while (true) {
       // warp 0: pop the first unexpanded entry, publish its row
       int nxt = 0;
+      int cur = -1;  // warp 0: prefetch buffer holding this expansion's row, or -1
       if (w == 0) {
         if (cursor < sz) {
           const uint32_t node = s.pool_id[cursor];
@@ -362,29 +363,33 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           // a predicted row (and its codes) is read where it was prefetched;
           // otherwise warp 0 copies the row to crow's half for this
           // expansion's parity
-          const int cur = node == pref_node ? pbuf : -1;
+          cur = node == pref_node ? pbuf : -1;
           if (cur < 0) {
             uint32_t* cw = s.crow + (it & 1) * a.r_pad;
             for (uint32_t i = lane; i < a.r_pad; i += 32) cw[i] = __ldg(a.adj + (size_t)node * a.r_pad + i);
           }
           if (lane == 0) s.ctl[8 + (it & 1)] = (uint32_t)(cur + 1);
-          __syncwarp();  // the pop mark and the row copy are visible to every lane
-          nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
-          const int nb = cur == 0 ? 1 : 0;  // the next in pool order; an early prediction takes the other
-          eb = 1 - nb;
-          if (nxt < sz) {
-            pref_node = s.pool_id[nxt] & ~kChecked;
-            if (use_fat) prefetch_fat(a.fat, a.r_pad, a.code_stride, s.fbuf + nb * fb_bytes, pref_node, lane, 32);
-            prefetch_row(a.adj, a.r_pad, s.rowbuf + nb * a.r_pad, pref_node, lane);
-            pbuf = nb;
-          } else {
-            pref_node = kSent;
-          }
         }
         if (lane == 0) s.ctl[it & 1] = cursor < sz ? 1u : 0u;
       }
       __syncthreads();
       if (s.ctl[it & 1] == 0) break;
+      if (w == 0) {
+        // while the other warps gather: the next unexpanded entry after this
+        // one, and the prefetch of its row (and codes) into the buffer this
+        // expansion does not read
+        nxt = find_unchecked(s.pool_id, cursor + 1, sz, lane);
+        const int nb = cur == 0 ? 1 : 0;  // the next in pool order; an early prediction takes the other
+        eb = 1 - nb;
+        if (nxt < sz) {
+          pref_node = s.pool_id[nxt] & ~kChecked;
+          if (use_fat) prefetch_fat(a.fat, a.r_pad, a.code_stride, s.fbuf + nb * fb_bytes, pref_node, lane, 32);
+          prefetch_row(a.adj, a.r_pad, s.rowbuf + nb * a.r_pad, pref_node, lane);
+          pbuf = nb;
+        } else {
+          pref_node = kSent;
+        }
+      }
       // the row: prefetch buffer + 1, or 0 for crow; the codes come from the
       // same buffer when they were prefetched with it
       const uint32_t rsel = s.ctl[8 + (it & 1)];
@@ -402,13 +407,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
         const uint32_t id = seg == 0 ? row[0] : seg == 1 ? row[1] : seg == 2 ? row[2] : row[3];
         const uint32_t sm = __ballot_sync(kFull, id == kSent);
         const int deg = sm ? __ffs(sm) - 1 : 32;
-        if (deg == 0) {
-          // the row ended at the previous segment; an empty row still takes
-          // one barrier, so that every warp has read it before warp 0 issues
-          // the next prefetch into its buffer
-          if (seg == 0) __syncthreads();
-          break;
-        }
+        if (deg == 0) break;  // the row ended at the previous segment
         const uint32_t par = segs_done & 1;
         uint32_t* cd = s.cand_d + 32 * par;
         ++segs_done;
@@ -573,7 +572,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
                 s.pool_d[j] = vd;
                 s.pool_id[j] = vi;
               }
-              __syncwarp();
+              // no sync here: a lower chunk reads only lower slots, and its
+              // own sync orders this chunk's reads before its writes
             }
             if (acc && cpos < (int)ef) {
               s.pool_d[cpos] = my_d;

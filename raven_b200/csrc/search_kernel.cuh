@@ -1096,7 +1096,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
                 s.pool_d[j] = vd;
                 s.pool_id[j] = vi;
               }
-              __syncwarp();
+              // no sync here: a lower chunk reads only lower slots, and its
+              // own sync orders this chunk's reads before its writes
             }
             if (acc && cpos < (int)ef) {
               s.pool_d[cpos] = my_d;
