@@ -670,6 +670,10 @@ def main():
     dev = DeviceIndex(g, base, device=dev_id, sq4=quant == 0, sq8=quant == 1, adaptive=True)
     if args.hash_bits or args.spill_bits:
         dev.set_tuning(hash_bits=args.hash_bits, spill_bits=args.spill_bits)
+    if args.no_extras:
+        # the timed batch kernel gathers codes: the copies stored beside the
+        # rows serve only the small-batch latency runs, which are skipped
+        dev.set_fat_rows(False)
     lib = L.load()
     nb, B, dim = qbatches.shape
     k = args.k
