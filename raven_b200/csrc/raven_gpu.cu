@@ -50,6 +50,9 @@ struct raven_index {
   // neighbour codes beside each row: node i's slot j holds the code of
   // adj[i][j] (zeros past the degree), n x r_pad x q_stride bytes, or null
   uint8_t* d_fat[2] = {nullptr, nullptr};
+  // SQ4: sum of the squared nibbles of each node's code (the search's
+  // distance is sum q^2 + sum x^2 - 2 sum qx, the last on tensor cores)
+  uint32_t* d_xnorm = nullptr;
   float* d_qparams[2] = {nullptr, nullptr};  // 5*dim
   std::vector<float> h_qparams[2];
   bool has_nav = false;
@@ -117,6 +120,21 @@ __global__ void fat_rows_kernel(const uint32_t* __restrict__ adj, const uint8_t*
       const uint32_t id = adj[row * r_pad + j];
       dst[t] = id == 0xFFFFFFFFu ? make_uint4(0, 0, 0, 0) : ((const uint4*)(codes + (size_t)id * stride))[pc];
     }
+  }
+}
+
+// Sum of squared nibbles of each SQ4 code row (padding nibbles are zero).
+__global__ void code_norms_kernel(const uint8_t* __restrict__ codes, uint64_t n, uint32_t stride,
+                                  uint32_t* __restrict__ out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t* w = (const uint32_t*)(codes + i * stride);
+    uint32_t acc = 0;
+    for (uint32_t j = 0; j < stride / 4; ++j) {
+      const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+      acc = __dp4a(lo, lo, acc);
+      acc = __dp4a(hi, hi, acc);
+    }
+    out[i] = acc;
   }
 }
 
@@ -715,6 +733,7 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
   a.hash_bits = pl.hash_bits;
   // neighbour codes beside the rows (read by the small-batch search without a visited set)
   a.fat = f32 ? nullptr : ix->d_fat[pl.quant];
+  a.xnorm = pl.quant == RAVEN_QUANT_SQ4 ? ix->d_xnorm : nullptr;
   a.spill_bits = pl.spill_bits;
   a.smem_per_warp = pl.smem_warp;
   a.f32_stage_rows = pl.f32_stage_rows;
@@ -895,6 +914,7 @@ void free_index(raven_index* ix) {
     cudaFree(ix->d_fat[q]);
     cudaFree(ix->d_qparams[q]);
   }
+  cudaFree(ix->d_xnorm);
   cudaFree(ix->d_nav_vec);
   cudaFree(ix->d_nav_e);
   cudaFree(ix->d_nav_gid);
@@ -1114,6 +1134,12 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
                                                           q == 0, stride, (uint32_t*)ix->d_codes[q]);
     if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "encode launch failed"));
     ix->has_q[q] = true;
+    if (q == 0) {
+      if (cudaMalloc((void**)&ix->d_xnorm, (size_t)n * 4) != cudaSuccess)
+        return bail2(fail(RAVEN_ENOMEM, "code norm allocation failed"));
+      code_norms_kernel<<<ix->num_sms * 8, 256, 0, ix->stream>>>(ix->d_codes[0], n, stride, ix->d_xnorm);
+      if (cudaGetLastError() != cudaSuccess) return bail2(fail(RAVEN_ECUDA, "code norm launch failed"));
+    }
     if ((rc = set_fat_rows(ix, q, true))) return bail2(rc);
   }
   // navigation layers: every node with an upper list gets a slot; its edges

@@ -117,6 +117,9 @@ struct SearchArgs {
   // neighbour codes beside each row (n x r_pad x code_stride), or null; read
   // by the small-batch kernel without a visited set
   const uint8_t* __restrict__ fat;
+  // SQ4: sum of squared nibbles per node (n entries): the batch kernel's
+  // tensor-core distance path needs it (always set for SQ4)
+  const uint32_t* __restrict__ xnorm;
 };
 
 // Per-warp shared-memory carve-up (every piece 16-byte aligned).
@@ -630,6 +633,18 @@ __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, 
   return sz;
 }
 
+// D += A (16 x 32 u8, row) x B (32 x 8 s8, col): the warp-level integer MMA,
+// exact. Fragments (thread t = 4 g + u): a0 = A[g][4u..4u+3], a1 = A[g+8][4u..],
+// a2 = A[g][16+4u..], a3 = A[g+8][16+4u..]; b0 = B[4u..4u+3][g], b1 =
+// B[16+4u..][g]; d0, d1 = D[g][2u, 2u+1], d2, d3 = D[g+8][2u, 2u+1].
+__device__ inline void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ inline uint32_t u4_word(const uint4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
 // dot product of 4 unsigned bytes (a) with 4 signed bytes (b), plus c.
 __device__ inline int dp4a_us(uint32_t a, int b, int c) {
   int d;
@@ -835,6 +850,17 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
       __syncwarp();  // the query code (and the table) are written before any lane reads them
       QChunk<QUANT> qc;
       qc.load(s.qcode, sub);
+      // SQ4 with four lanes per code and a run-time pool (ef > 64): a row's
+      // distances on the tensor cores as sum q^2 + sum x^2 - 2 sum qx (exact
+      // integers): sum q^2 over all four chunks here, sum x^2 per node from
+      // the upload. (Measured: 5.78 -> 6.11 M QPS at ef=140; with the fixed
+      // 64-entry pool, ef <= 64, the dp4a path stays faster.)
+      constexpr bool kMma = QUANT == 0 && CPL == 4 && POOLMAX == 0;
+      int qqf = 0;
+      if constexpr (kMma) {
+        qqf = qc.qq + __shfl_xor_sync(kFull, qc.qq, 1);
+        qqf += __shfl_xor_sync(kFull, qqf, 2);
+      }
 
       int level = 0;
       uint32_t tcount = 0, scount = 0;
@@ -929,6 +955,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
           // rows hold no repeated id (the upload drops later repeats, which the
           // reference treats as already visited), so every valid lane probes.
           const bool valid = lane < deg;
+          const uint32_t xn = (kMma && valid) ? __ldg(a.xnorm + id) : 0u;
           bool is_new = false;
           uint32_t newm = 0;  // lanes holding a first visit
           if (VIS) {
@@ -1001,6 +1028,38 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
             rows_dist(s.qf, s.fstage, a.f32_stage_rows, s.cand_id, __popc(newm), a.dim, a.vec_c, a.vec_rem, vec_row,
                       s.nd, lane);
             my_d = is_new ? __float_as_uint(s.nd[cpos]) : 0xffffffffu;
+          } else if constexpr (kMma) {
+            // the row's 32 codes as two 16 x 128 tiles (rounds 0-1, 2-3: row
+            // m of tile t is neighbour 16 t + m) against -2q: K block kb takes
+            // word kb of every lane's 16-byte chunk, low nibbles as columns
+            // 4u.., high nibbles as 16 + 4u.. (the same order for the query)
+            // (two accumulators per tile, even and odd K blocks, halve the
+            // dependent MMA chain)
+            int t0[4] = {0, 0, 0, 0}, t1[4] = {0, 0, 0, 0}, u0[4] = {0, 0, 0, 0}, u1[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              const uint32_t w0 = u4_word(data[0], kb), w1 = u4_word(data[1 % CPL], kb);
+              const uint32_t w2 = u4_word(data[2 % CPL], kb), w3 = u4_word(data[3 % CPL], kb);
+              const uint32_t m = 0x0F0F0F0Fu;
+              const uint32_t b0 = (uint32_t)qc.m2q_lo[kb], b1 = (uint32_t)qc.m2q_hi[kb];
+              if (kb & 1) {
+                mma_u8s8(u0, w0 & m, w1 & m, (w0 >> 4) & m, (w1 >> 4) & m, b0, b1);
+                mma_u8s8(u1, w2 & m, w3 & m, (w2 >> 4) & m, (w3 >> 4) & m, b0, b1);
+              } else {
+                mma_u8s8(t0, w0 & m, w1 & m, (w0 >> 4) & m, (w1 >> 4) & m, b0, b1);
+                mma_u8s8(t1, w2 & m, w3 & m, (w2 >> 4) & m, (w3 >> 4) & m, b0, b1);
+              }
+            }
+            t0[0] += u0[0];
+            t0[2] += u0[2];
+            t1[0] += u1[0];
+            t1[2] += u1[2];
+            // neighbour `lane`: tile lane >> 4, row lane & 15, held by thread 4 (lane & 7)
+            const int src = (lane & 7) << 2;
+            const int e0 = __shfl_sync(kFull, t0[0], src), e1 = __shfl_sync(kFull, t0[2], src);
+            const int e2 = __shfl_sync(kFull, t1[0], src), e3 = __shfl_sync(kFull, t1[2], src);
+            const int dot = lane < 16 ? ((lane & 8) ? e1 : e0) : ((lane & 8) ? e3 : e2);
+            my_d = (VIS ? is_new : valid) ? (uint32_t)(qqf + (int)xn + dot) : 0xffffffffu;
           } else {
             // integer distances of the row (candidate idx -> cand_d[idx])
 #pragma unroll
