@@ -66,11 +66,6 @@ struct raven_index {
   int hash_bits_override = 0;
   int spill_bits_override = 0;
   uint64_t small_batch_max = ~0ull;  // batches of at most this many queries run one CTA per query (~0: one wave)
-  // host-buffer searches: queries are copied in pieces on this stream while
-  // the search runs; h_piece_counts[c] = c + 1 (pinned) is what the copy
-  // engine writes to the device's pieces-delivered counter after piece c
-  cudaStream_t copy_stream = nullptr;
-  uint32_t* h_piece_counts = nullptr;
 };
 
 namespace {
@@ -686,11 +681,7 @@ cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, bool vis, uint32_t sm
 }
 
 constexpr int kCtaAutoPerSm = 4;  // small-batch kernel: default limit, resident CTAs per SM
-// host-buffer searches of at least kPieceMinQueries queries copy them in at
-// most kMaxQueryPieces pieces (of at least kMinPieceQueries) while the search runs
-constexpr uint64_t kPieceMinQueries = 2048;
-constexpr uint32_t kMaxQueryPieces = 64;
-constexpr uint64_t kMinPieceQueries = 1024;
+
 constexpr uint32_t kMaxEf = 256;
 constexpr uint32_t kMaxDimSq4 = 256;
 constexpr uint32_t kMaxDimSq8 = 128;
@@ -904,53 +895,8 @@ int run_search_cta(raven_index* ix, const float* d_q, uint64_t nq, const raven_s
 }
 
 // Runs the search (or the nav-only descent) for device buffers.
-// Queries still being copied to the device (host-buffer calls): the batch
-// kernel waits per query on `ready`; `after_launch` enqueues the pieces not
-// yet issued and records `delivered` once all are; any other kernel waits for
-// `delivered` before it starts.
-struct QueryFeed {
-  const uint32_t* ready;
-  uint32_t piece;
-  uint32_t* err;
-  cudaEvent_t delivered;
-  void (*after_launch)(void*);
-  void* ctx;
-};
-
-// Issues the query pieces of a host-buffer search on the index's copy stream:
-// piece c's rows, then h_piece_counts[c] (= c + 1) into the delivered
-// counter; `issue` sends the pieces from `next` on and records `delivered`
-// (once; later calls do nothing).
-struct PieceFeeder {
-  raven_index* ix;
-  const float* h_q;
-  float* d_q;
-  uint64_t nq, piece;
-  uint32_t* d_count;
-  cudaEvent_t delivered;
-  uint64_t next = 0;
-  bool done = false;
-  cudaError_t err = cudaSuccess;
-  void send(uint64_t c) {
-    const uint64_t q0 = c * piece, qn = std::min(piece, nq - q0);
-    const size_t row = (size_t)ix->dim * 4;
-    if (err == cudaSuccess)
-      err = cudaMemcpyAsync(d_q + q0 * ix->dim, h_q + q0 * ix->dim, qn * row, cudaMemcpyHostToDevice, ix->copy_stream);
-    if (err == cudaSuccess)
-      err = cudaMemcpyAsync(d_count, ix->h_piece_counts + c, 4, cudaMemcpyHostToDevice, ix->copy_stream);
-  }
-  uint64_t pieces() const { return (nq + piece - 1) / piece; }
-  static void issue(void* self) {
-    PieceFeeder& f = *(PieceFeeder*)self;
-    if (f.done) return;
-    for (; f.next < f.pieces(); ++f.next) f.send(f.next);
-    if (f.err == cudaSuccess) f.err = cudaEventRecord(f.delivered, f.ix->copy_stream);
-    f.done = true;
-  }
-};
-
 int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_search_params* p,
-               const raven_search_outputs* o, cudaStream_t st, int nav_only, const QueryFeed* feed = nullptr) {
+               const raven_search_outputs* o, cudaStream_t st, int nav_only) {
   Plan pl;
   raven_search_params nav_p{};
   if (nav_only) {
@@ -977,13 +923,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
       // takes over between 3 and 6 resident CTAs per SM
       lim = (uint64_t)std::min(std::max(per_sm, 0), kCtaAutoPerSm) * (uint64_t)ix->num_sms;
     }
-    if (nq <= lim) {
-      if (feed) {
-        feed->after_launch(feed->ctx);
-        CU(cudaStreamWaitEvent(st, feed->delivered, 0));
-      }
-      return run_search_cta(ix, d_q, nq, p, pl, o, st);
-    }
+    if (nq <= lim) return run_search_cta(ix, d_q, nq, p, pl, o, st);
   }
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
@@ -1021,13 +961,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   a.rerank_f16 = (!nav_only && p->rerank_f16) ? 1 : 0;
   a.counter = counter;
   a.nav_only = nav_only;
-  if (feed) {
-    a.q_ready = feed->ready;
-    a.q_piece = feed->piece;
-    a.q_err = feed->err;
-  }
   e = dispatch(pl.quant, pl.cpl, vis, false, a, pl.smem_block, grid, st, nullptr);
-  if (feed) feed->after_launch(feed->ctx);
   cudaFreeAsync(scratch, st);
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search launch: ") + cudaGetErrorString(e));
   return RAVEN_OK;
@@ -1080,8 +1014,6 @@ void free_index(raven_index* ix) {
   cudaFree(ix->d_nav_gid);
   cudaFree(ix->d_samples);
   if (ix->stream) cudaStreamDestroy(ix->stream);
-  if (ix->copy_stream) cudaStreamDestroy(ix->copy_stream);
-  if (ix->h_piece_counts) cudaFreeHost(ix->h_piece_counts);
   delete ix;
 }
 
@@ -1233,10 +1165,7 @@ int raven_index_upload(const raven_graph* gr, const float* vectors, uint64_t n, 
       cudaStreamCreateWithFlags(&ix->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(fail(RAVEN_ECUDA, "device query / stream creation failed"));
   ix->small_batch_max = ~0ull;  // one wave of CTAs (resolved per call)
-  if (cudaStreamCreateWithFlags(&ix->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaHostAlloc((void**)&ix->h_piece_counts, kMaxQueryPieces * 4, cudaHostAllocDefault) != cudaSuccess)
-    return bail(fail(RAVEN_ECUDA, "copy stream / pinned counter allocation failed"));
-  for (uint32_t c = 0; c < kMaxQueryPieces; ++c) ix->h_piece_counts[c] = c + 1;
+
   {
     // per-call scratch comes from the device's stream-ordered pool; keep freed
     // blocks cached instead of returning them to the driver at every sync
@@ -1443,10 +1372,6 @@ int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven
   const size_t o_e = out->ef_used ? take(nq * 4) : 0, o_s = out->status ? take(nq * 4) : 0;
   const size_t o_n = out->n_nav ? take(nq * 4) : 0, o_x = out->expansions ? take(nq * 4) : 0;
   const size_t o_h = hc ? take(nq * hc * 4) : 0, o_hl = hc ? take(nq * 4) : 0;
-  // large batches: the queries go over in pieces on the copy stream while the
-  // search runs (counter of pieces delivered, wait-timeout flag)
-  const bool in_pieces = nq >= kPieceMinQueries && ix->copy_stream && ix->h_piece_counts;
-  const size_t o_f = in_pieces ? take(8) : 0;
   uint8_t* buf = nullptr;
   CU(cudaMallocAsync((void**)&buf, off, st));
   raven_search_outputs d{};
@@ -1462,34 +1387,9 @@ int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven
   d.history_cap = (uint32_t)hc;
   d.history_len = hc ? (uint32_t*)(buf + o_hl) : nullptr;
   int rc = RAVEN_OK;
-  cudaError_t e = cudaSuccess;
-  if (hc) e = cudaMemsetAsync(d.history, 0, nq * hc * 4, st);  // entries past history_len read 0
-  uint32_t* flags = (uint32_t*)(buf + o_f);
-  uint32_t h_timeout = 0;
-  cudaEvent_t ev_alloc = nullptr, ev_delivered = nullptr;
-  if (!in_pieces) {
-    if (e == cudaSuccess) e = cudaMemcpyAsync(buf + o_q, q, nq * ix->dim * 4, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) rc = run_search(ix, (const float*)(buf + o_q), nq, p, &d, st, 0);
-  } else {
-    if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, 8, st);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_alloc, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev_delivered, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventRecord(ev_alloc, st);  // the buffer and the zeroed counter exist
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(ix->copy_stream, ev_alloc, 0);
-    if (e == cudaSuccess) {
-      PieceFeeder fd{ix, q, (float*)(buf + o_q), nq,
-                     std::max<uint64_t>(kMinPieceQueries, (nq + kMaxQueryPieces - 1) / kMaxQueryPieces), flags,
-                     ev_delivered};
-      fd.send(0);  // the first piece goes before the launch
-      fd.next = 1;
-      QueryFeed feed{flags, (uint32_t)fd.piece, flags + 1, ev_delivered, &PieceFeeder::issue, &fd};
-      rc = run_search(ix, (const float*)(buf + o_q), nq, p, &d, st, 0, &feed);
-      PieceFeeder::issue(&fd);  // when the search stopped before its launch
-      e = fd.err;
-      // the results, the buffer's release and the timeout flag follow every piece
-      if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ev_delivered, 0);
-    }
-  }
+  cudaError_t e = cudaMemcpyAsync(buf + o_q, q, nq * ix->dim * 4, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && hc) e = cudaMemsetAsync(d.history, 0, nq * hc * 4, st);  // entries past history_len read 0
+  if (e == cudaSuccess) rc = run_search(ix, (const float*)(buf + o_q), nq, p, &d, st, 0);
   auto back = [&](void* dst, const void* src, size_t bytes) {
     if (dst && e == cudaSuccess) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, st);
   };
@@ -1506,14 +1406,10 @@ int raven_search_batch(raven_index* ix, const float* q, uint64_t nq, const raven
       back(out->history, d.history, nq * hc * 4);
       back(out->history_len, d.history_len, nq * 4);
     }
-    if (in_pieces) back(&h_timeout, flags + 1, 4);
   }
   cudaFreeAsync(buf, st);
   cudaError_t es = cudaStreamSynchronize(st);
-  if (ev_alloc) cudaEventDestroy(ev_alloc);
-  if (ev_delivered) cudaEventDestroy(ev_delivered);
   if (rc) return rc;
-  if (h_timeout) return fail(RAVEN_ECUDA, "search: the query upload did not arrive within the wait bound");
   if (e != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search copies: ") + cudaGetErrorString(e));
   if (es != cudaSuccess) return fail(RAVEN_ECUDA, std::string("search: ") + cudaGetErrorString(es));
   return RAVEN_OK;

@@ -57,20 +57,6 @@ constexpr int kWarpsPerBlock = 4;
 constexpr int kMinBlocksPerSm = 6;  // 80 registers/thread: the measured best residency trade-off
 constexpr int kMinBlocksPerSmPool = 7;  // without a visited set: 72 registers, 7 blocks (measured best of 6/7/8)
 constexpr uint32_t kNavStepLimit = 1u << 16;
-constexpr uint32_t kPieceWaitLimit = 1u << 22;  // polls of ~256 ns: about a second
-
-// Waits until *ready >= need (a counter the copy engine writes after each
-// piece of the queries it delivers). Bounded: returns false after
-// kPieceWaitLimit polls.
-__device__ inline bool wait_for_piece(const uint32_t* ready, uint32_t need) {
-  for (uint32_t it = 0; it < kPieceWaitLimit; ++it) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ready) : "memory");
-    if (v >= need) return true;
-    __nanosleep(256);
-  }
-  return false;
-}
 
 struct SearchArgs {
   // index
@@ -134,12 +120,6 @@ struct SearchArgs {
   // SQ4: sum of squared nibbles per node (n entries): the batch kernel's
   // tensor-core distance path needs it (always set for SQ4)
   const uint32_t* __restrict__ xnorm;
-  // queries still arriving (host-buffer calls): the copy engine writes the
-  // number of q_piece-query pieces delivered to *q_ready after each piece; a
-  // warp waits (bounded) for its query's piece and reports a timeout in *q_err
-  const uint32_t* q_ready;
-  uint32_t q_piece;
-  uint32_t* q_err;
 };
 
 // Per-warp shared-memory carve-up (every piece 16-byte aligned).
@@ -775,18 +755,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
     const uint64_t qi = __shfl_sync(kFull, qi_, 0);
     if (qi >= a.nq) break;
 
-    // 1. query -> shared memory (lane-major), once its piece has arrived;
-    // read past L1 (a line can hold the start of a later, not yet delivered query)
-    bool q_ok = true;
-    if (a.q_ready) {
-      uint32_t ok = 1;
-      if (lane == 0) ok = wait_for_piece(a.q_ready, (uint32_t)(qi / a.q_piece) + 1u) ? 1u : 0u;
-      q_ok = __shfl_sync(kFull, ok, 0) != 0;
-      if (!q_ok && lane == 0) atomicExch(a.q_err, 1u);
-    }
+    // 1. query -> shared memory (lane-major)
     const float* qg = a.queries + qi * a.dim;
     for (uint32_t i = lane; i < a.dim_pad; i += 32) {
-      if (i < a.dim) s.qf[lane_major_pos(i, a.vec_c)] = q_ok ? __ldcg(qg + i) : 0.0f;
+      if (i < a.dim) s.qf[lane_major_pos(i, a.vec_c)] = qg[i];
       else s.qf[i] = 0.0f;
     }
     __syncwarp();
