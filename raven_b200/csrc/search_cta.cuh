@@ -510,7 +510,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           bool acc = cand && (!full || my_d < worst);
           int lo = 0;  // # pool entries <= my_d (ties: pool first)
           if (acc) {
-            lo = pool_upper_bound(s.pool_d, sz, my_d);
+            lo = pool_upper_bound4(s.pool_d, sz, my_d);
             // without the visited set: a neighbour already in the pool sits
             // in the run of equal distances ending at lo - 1
             if (!VIS)
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           }
           const uint32_t am = __ballot_sync(kFull, acc);
           const int na = __popc(am);
-          __syncwarp();
+          // (no sync needed here: the chunk moves sync before their first write)
           if (na > 0) {
             int cpos = acc ? lo : 0x7fffffff;
             const int start = (int)__reduce_min_sync(kFull, (unsigned)cpos);

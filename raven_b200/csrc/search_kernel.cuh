@@ -623,6 +623,21 @@ __device__ inline int pool_upper_bound(const uint32_t* pool_d, int sz, uint32_t 
   return pos;
 }
 
+// The same count in four steps of three independent shared reads each (for a
+// latency-bound caller: half the dependent chain of pool_upper_bound).
+__device__ inline int pool_upper_bound4(const uint32_t* pool_d, int sz, uint32_t d) {
+  int pos = 0;
+#pragma unroll
+  for (int step = 64; step > 0; step >>= 2) {
+    const int p1 = pos + step, p2 = pos + 2 * step, p3 = pos + 3 * step;
+    const bool c1 = p1 <= sz && pool_d[p1 - 1] <= d;
+    const bool c2 = p2 <= sz && pool_d[p2 - 1] <= d;
+    const bool c3 = p3 <= sz && pool_d[p3 - 1] <= d;
+    pos += step * ((int)c1 + (int)c2 + (int)c3);
+  }
+  return pos;
+}
+
 __device__ inline int find_unchecked(const uint32_t* pool_id, int from, int sz, int lane) {
   for (int base = from & ~31; base < sz; base += 32) {
     const int p = base + lane;
@@ -1094,7 +1109,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
           }
           const uint32_t am = __ballot_sync(kFull, acc);
           const int na = __popc(am);
-          __syncwarp();
+          // (no sync needed here: the chunk moves sync before their first write)
           if (na > 0) {
             // pool entries from the first insertion point onward move right
             int cpos = 0x7fffffff;
