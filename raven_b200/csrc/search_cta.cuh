@@ -10,11 +10,13 @@
 //     as in the batch kernel). VIS false: no visited set; pool membership
 //     decides new neighbours, with the same results (the argument is in
 //     search_kernel.cuh), and a CTA needs only its pool and staging rows;
-//   * the four warps share each expansion's work: every warp gathers the
-//     codes of eight of the row's neighbours and computes their distances,
-//     while warp 0 also runs the visited set and then the pool merge; the
-//     navigation descent and the rerank stage and score 16 rows per round
-//     across the warps.
+//   * the four warps share each expansion's work: with the visited set every
+//     warp gathers the codes of eight of the row's neighbours and computes
+//     their distances while warp 0 also runs the visited set; without it
+//     warps 1-3 take eleven each while warp 0 finds the next unexpanded entry
+//     and issues its prefetch; warp 0 then merges the pool. The navigation
+//     descent and the rerank stage and score 16 rows per round across the
+//     warps.
 // The search itself is the batch kernel's (search_kernel.cuh): the same
 // navigation descent, AdaptiveEf rank lookup, visited order, LinearPool merge
 // and rerank tie rule, so results are identical (src/graph/vamana.rs:786-861,
@@ -216,7 +218,13 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
   const uint32_t SB = S << 3;
   const uint32_t sb_limit = (SB >> 2) * 3;
   constexpr int CPR = 32 / CPL;                              // codes per warp round
-  constexpr int ROUNDS = CPR >= 8 ? 1 : 8 / CPR;             // rounds for a warp's eight neighbours
+  // neighbours a gathering warp scores per segment: with the visited set all
+  // four warps take eight (warp 0 also runs the visited set); without it
+  // warps 1-3 take eleven, and warp 0 meanwhile finds the next entry and
+  // issues its prefetch
+  constexpr int kPer = VIS ? 8 : 11;
+  constexpr int ROUNDS = (kPer + CPR - 1) / CPR;              // rounds for a warp's share
+  const int gw = VIS ? w : w - 1;                             // gathering-warp index, -1: none
   const int sub = lane & (CPL - 1);
   const int grp = lane / CPL;
   auto vec_row = [&](uint32_t id) -> const float* { return a.vec + (size_t)id * a.dim; };
@@ -411,14 +419,18 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
         const uint32_t par = segs_done & 1;
         uint32_t* cd = s.cand_d + 32 * par;
         ++segs_done;
-        // every warp: codes of neighbours 8w .. 8w+7 of this segment
+        // gathering warps: codes of neighbours kPer gw .. kPer gw + kPer - 1 of this segment
         uint4 data[ROUNDS];
         int idxr[ROUNDS];
 #pragma unroll
         for (int r = 0; r < ROUNDS; ++r) {
-          const int loc = r * CPR + grp;  // neighbour within this warp's eight
-          const int idx = 8 * w + loc;
-          idxr[r] = (loc < 8 && idx < deg) ? idx : -1;
+          const int loc = r * CPR + grp;  // neighbour within this warp's share
+          const int idx = kPer * gw + loc;
+          idxr[r] = (gw >= 0 && loc < kPer && idx < deg) ? idx : -1;
+          if (gw < 0) {  // warp 0 without the visited set: no share
+            data[r] = make_uint4(0, 0, 0, 0);
+            continue;
+          }
           const uint32_t cid = __shfl_sync(kFull, id, idx & 31);
           const uint32_t c = idxr[r] >= 0 ? cid : 0u;  // address always in range
           if (seg == 0 && fsel != 0)  // the prefetched copy (slot idx & 31 is always in the buffer)
@@ -488,9 +500,10 @@ __global__ void __launch_bounds__(kCtaThreads, 1) search_cta_kernel(const Search
           vcount += nn;
           if (lane == 0) s.ctl[2 + par] = overflow ? 1u : 0u;
         }
-        // every warp: distances of its eight neighbours
+        // gathering warps: distances of their share
 #pragma unroll
         for (int r = 0; r < ROUNDS; ++r) {
+          if (gw < 0) break;
           int pdist = qc.dist(data[r]);
 #pragma unroll
           for (int o = 1; o < CPL; o <<= 1) pdist += __shfl_xor_sync(kFull, pdist, o);
