@@ -7,8 +7,10 @@
 //   3. AdaptiveEf rank -> ef table lookup, .max(k)      (src/graph/adaptive_ef.rs:340-359,
 //                                                        src/graph/vamana.rs:1803)
 //   4. beam search over the fixed-degree adjacency      (src/graph/vamana.rs:786-861 / 683-773,
-//      with an exact visited set and the LinearPool     src/graph/linear_pool.rs:100-171,
-//      ordering                                         src/memory/visited.rs:88-103)
+//      with the LinearPool ordering; new neighbours     src/graph/linear_pool.rs:100-171,
+//      by pool membership or an exact visited set        src/memory/visited.rs:88-103)
+//      (VIS below); SQ4 distances of a row on the
+//      tensor cores when the pool is run-time sized
 //   5. f32 rerank of min(k*rr, |pool|) survivors        (src/graph/refiner.rs:45-61)
 //
 // QUANT selects the beam's distance: 0 SQ4 codes, 1 SQ8 codes, 2 the f32
