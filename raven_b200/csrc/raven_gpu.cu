@@ -545,18 +545,47 @@ struct MergeLayout {
   __device__ uint64_t block(uint32_t s) const { return (uint64_t)(s % W) * P + s / W; }
 };
 
+constexpr uint32_t kMergeStage = 256;  // candidates per query staged in shared memory (n_shards * k)
+constexpr int kMergeThreads = 256;
+
 __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float* __restrict__ ds,
                                    const uint32_t* __restrict__ counts, MergeLayout L, uint32_t n_shards, uint64_t nq,
                                    uint32_t k, uint64_t shard_size, uint32_t* __restrict__ out_i,
                                    float* __restrict__ out_d, uint32_t* __restrict__ out_c) {
+  __shared__ float merge_stage[kMergeThreads / 32][kMergeStage];
   const uint64_t qi = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (qi >= nq) return;
+  if (qi >= nq) return;  // whole warps
   const uint32_t total = n_shards * k;
   auto cnt_of = [&](uint32_t sh) { return counts ? min(counts[L.block(sh) * L.stride_c + qi], k) : k; };
   auto dist_at = [&](uint32_t sh, uint32_t r) { return ds[L.block(sh) * L.stride_d + qi * k + r]; };
   uint32_t valid_total = 0;
   for (uint32_t sh = 0; sh < n_shards; ++sh) valid_total += cnt_of(sh);
+  if (total <= kMergeStage) {
+    // the query's candidates staged once, in shard-major order (entry e =
+    // shard e / k, rank e % k); entries past a shard's count are NaN, which
+    // no comparison counts. Ties by (distance, shard, rank) = (distance, e).
+    float* sd = merge_stage[threadIdx.x >> 5];
+    for (uint32_t e = lane; e < total; e += 32) {
+      const uint32_t sh = e / k, r = e - sh * k;
+      sd[e] = r < cnt_of(sh) ? dist_at(sh, r) : __int_as_float(0x7fc00000);
+    }
+    __syncwarp();
+    for (uint32_t e = lane; e < total; e += 32) {
+      const float d = sd[e];
+      if (d != d) continue;  // past its shard's count
+      uint32_t rank = 0;
+      for (uint32_t f = 0; f < total; ++f) {
+        const float df = sd[f];
+        rank += (df < d) || (df == d && f < e);
+      }
+      if (rank < k) {
+        const uint32_t sh = e / k, r = e - sh * k;
+        out_i[qi * k + rank] = (uint32_t)(sh * shard_size + ids[L.block(sh) * L.stride_i + qi * k + r]);
+        out_d[qi * k + rank] = d;
+      }
+    }
+  } else {
   for (uint32_t e = lane; e < total; e += 32) {
     const uint32_t sh = e / k, r = e % k;
     if (r >= cnt_of(sh)) continue;
@@ -573,6 +602,7 @@ __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float
       out_d[qi * k + rank] = d;
     }
   }
+  }
   const uint32_t outc = min(valid_total, k);
   for (uint32_t r = outc + lane; r < k; r += 32) {
     out_i[qi * k + r] = 0;
@@ -584,9 +614,18 @@ __global__ void shard_merge_kernel(const uint32_t* __restrict__ ids, const float
 // ---------------------------------------------------------------------------
 // Search launch.
 // ---------------------------------------------------------------------------
+// The instantiation for a launch: fixed 64-entry pool, run-time pool, or (SQ4
+// with four lanes per code, when the host enabled it through a.xnorm) the
+// run-time pool with tensor-core distances.
+template <int QUANT, int CPL, bool VIS>
+auto search_variant(uint32_t pool_cap, bool mma) {
+  if constexpr (QUANT == 0 && CPL == 4)
+    if (pool_cap > 64 && mma) return search_kernel<QUANT, CPL, 0, VIS, true>;
+  return pool_cap <= 64 ? search_kernel<QUANT, CPL, 64, VIS> : search_kernel<QUANT, CPL, 0, VIS>;
+}
 template <int QUANT, int CPL, bool VIS>
 cudaError_t launch_t(const SearchArgs& a, uint32_t smem_per_block, int grid, cudaStream_t st) {
-  auto k = a.pool_cap <= 64 ? search_kernel<QUANT, CPL, 64, VIS> : search_kernel<QUANT, CPL, 0, VIS>;
+  auto k = search_variant<QUANT, CPL, VIS>(a.pool_cap, a.xnorm != nullptr);
   cudaError_t e = allow_smem((const void*)k, smem_per_block);
   if (e != cudaSuccess) return e;
   k<<<grid, kWarpsPerBlock * 32, smem_per_block, st>>>(a);
@@ -600,8 +639,8 @@ cudaError_t launch_t(const SearchArgs& a, uint32_t smem_per_block, int grid, cud
   return e;
 }
 template <int QUANT, int CPL, bool VIS>
-cudaError_t occupancy_t(uint32_t pool_cap, uint32_t smem_per_block, int* blocks) {
-  auto k = pool_cap <= 64 ? search_kernel<QUANT, CPL, 64, VIS> : search_kernel<QUANT, CPL, 0, VIS>;
+cudaError_t occupancy_t(uint32_t pool_cap, bool mma, uint32_t smem_per_block, int* blocks) {
+  auto k = search_variant<QUANT, CPL, VIS>(pool_cap, mma);
   return blocks_per_sm((const void*)k, kWarpsPerBlock * 32, smem_per_block, blocks);
 }
 
@@ -610,13 +649,17 @@ cudaError_t dispatch_cpl(int cpl, bool occ, const SearchArgs& a, uint32_t smem, 
                          int* blocks) {
   switch (cpl) {
     case 1:
-      return occ ? occupancy_t<QUANT, 1, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 1, VIS>(a, smem, grid, st);
+      return occ ? occupancy_t<QUANT, 1, VIS>(a.pool_cap, a.xnorm != nullptr, smem, blocks)
+                 : launch_t<QUANT, 1, VIS>(a, smem, grid, st);
     case 2:
-      return occ ? occupancy_t<QUANT, 2, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 2, VIS>(a, smem, grid, st);
+      return occ ? occupancy_t<QUANT, 2, VIS>(a.pool_cap, a.xnorm != nullptr, smem, blocks)
+                 : launch_t<QUANT, 2, VIS>(a, smem, grid, st);
     case 4:
-      return occ ? occupancy_t<QUANT, 4, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 4, VIS>(a, smem, grid, st);
+      return occ ? occupancy_t<QUANT, 4, VIS>(a.pool_cap, a.xnorm != nullptr, smem, blocks)
+                 : launch_t<QUANT, 4, VIS>(a, smem, grid, st);
     case 8:
-      return occ ? occupancy_t<QUANT, 8, VIS>(a.pool_cap, smem, blocks) : launch_t<QUANT, 8, VIS>(a, smem, grid, st);
+      return occ ? occupancy_t<QUANT, 8, VIS>(a.pool_cap, a.xnorm != nullptr, smem, blocks)
+                 : launch_t<QUANT, 8, VIS>(a, smem, grid, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -626,7 +669,7 @@ cudaError_t dispatch_cpl(int cpl, bool occ, const SearchArgs& a, uint32_t smem, 
 cudaError_t dispatch(int quant, int cpl, bool vis, bool occ, const SearchArgs& a, uint32_t smem, int grid,
                      cudaStream_t st, int* blocks) {
   if (quant == RAVEN_QUANT_F32)
-    return occ ? occupancy_t<2, 1, true>(a.pool_cap, smem, blocks) : launch_t<2, 1, true>(a, smem, grid, st);
+    return occ ? occupancy_t<2, 1, true>(a.pool_cap, false, smem, blocks) : launch_t<2, 1, true>(a, smem, grid, st);
   if (vis)
     return quant == 0 ? dispatch_cpl<0, true>(cpl, occ, a, smem, grid, st, blocks)
                       : dispatch_cpl<1, true>(cpl, occ, a, smem, grid, st, blocks);
@@ -681,6 +724,8 @@ cudaError_t dispatch_cta_cpl(int cpl, const SearchArgs& a, bool vis, uint32_t sm
 }
 
 constexpr int kCtaAutoPerSm = 4;  // small-batch kernel: default limit, resident CTAs per SM
+constexpr uint32_t kMmaMaxPool = 160;        // tensor-core distances: largest pool
+constexpr uint64_t kMmaMaxNodes = 4u << 20;  // ... and largest index (16 MB of norms)
 
 constexpr uint32_t kMaxEf = 256;
 constexpr uint32_t kMaxDimSq4 = 256;
@@ -777,6 +822,17 @@ int make_plan(const raven_index* ix, const raven_search_params* p, Plan* pl) {
   return RAVEN_OK;
 }
 
+// The per-node code norms when a batch launch should use the tensor-core SQ4
+// distances (the instantiation is chosen from them), else null (dp4a).
+// Measured faster for pools of up to 160 entries while the norms stay in L2
+// (1M nodes: ef 100-160 +4-5 %); slower at ef 200 (-14 %) and on 10M nodes,
+// whose 40 MB of norms cost a DRAM sector per neighbour (-4 % at ef 100).
+const uint32_t* mma_norms(const raven_index* ix, const Plan& pl) {
+  const bool on = pl.quant == RAVEN_QUANT_SQ4 && pl.cpl == 4 && pl.pool_cap > 64 && pl.pool_cap <= kMmaMaxPool &&
+                  ix->n <= kMmaMaxNodes;
+  return on ? ix->d_xnorm : nullptr;
+}
+
 // Kernel arguments shared by every search launch (the caller sets the
 // queries, the scratch areas and the work counter).
 void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params* p, const raven_search_outputs* o,
@@ -827,7 +883,7 @@ void fill_args(const raven_index* ix, const Plan& pl, const raven_search_params*
   a.hash_bits = pl.hash_bits;
   // neighbour codes beside the rows (read by the small-batch search without a visited set)
   a.fat = f32 ? nullptr : ix->d_fat[pl.quant];
-  a.xnorm = pl.quant == RAVEN_QUANT_SQ4 ? ix->d_xnorm : nullptr;
+  a.xnorm = mma_norms(ix, pl);
   a.spill_bits = pl.spill_bits;
   a.smem_per_warp = pl.smem_warp;
   a.f32_stage_rows = pl.f32_stage_rows;
@@ -928,6 +984,7 @@ int run_search(raven_index* ix, const float* d_q, uint64_t nq, const raven_searc
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
+  occ_args.xnorm = mma_norms(ix, pl);
   const bool vis = nav_only || needs_visited(pl.quant, o);
   CU(dispatch(pl.quant, pl.cpl, vis, true, occ_args, pl.smem_block, 0, st, &blocks_per_sm));
   if (blocks_per_sm <= 0) return fail(RAVEN_ELIMIT, "search kernel does not fit on an SM with this configuration");
@@ -1621,9 +1678,9 @@ int raven_merge_topk_device(const uint32_t* d_ids, const float* d_dists, const u
   if (nq == 0) return RAVEN_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const MergeLayout lay{1u, n_shards, nq * k, nq * k, nq};
-  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(d_ids, d_dists, d_counts, lay, n_shards, nq,
-                                                                        k, shard_size, d_out_ids, d_out_dists,
-                                                                        d_out_counts);
+  const unsigned blocks = (unsigned)((nq * 32 + kMergeThreads - 1) / kMergeThreads);
+  shard_merge_kernel<<<blocks, kMergeThreads, 0, st>>>(d_ids, d_dists, d_counts, lay, n_shards, nq, k, shard_size,
+                                                       d_out_ids, d_out_dists, d_out_counts);
   CU(cudaGetLastError());
   return RAVEN_OK;
 }
@@ -1641,7 +1698,8 @@ int raven_merge_topk_gathered_device(const void* d_gathered, uint32_t n_shards, 
   const uint64_t block = nq * (2ull * k + 1);  // words per shard block: ids, distances, counts
   const uint32_t* base = (const uint32_t*)d_gathered;
   const MergeLayout lay{world, per_rank, block, block, block};
-  shard_merge_kernel<<<(unsigned)((nq * 32 + 255) / 256), 256, 0, st>>>(
+  const unsigned blocks = (unsigned)((nq * 32 + kMergeThreads - 1) / kMergeThreads);
+  shard_merge_kernel<<<blocks, kMergeThreads, 0, st>>>(
       base, (const float*)(base + nq * k), base + 2 * nq * k, lay, n_shards, nq, k, shard_size, d_out_ids, d_out_dists,
       d_out_counts);
   CU(cudaGetLastError());
@@ -1756,6 +1814,7 @@ int raven_search_batch_device_noalloc(raven_index* ix, const float* d_q, uint64_
   int blocks_per_sm = 0;
   SearchArgs occ_args{};
   occ_args.pool_cap = pl.pool_cap;  // selects the kernel variant whose occupancy is asked
+  occ_args.xnorm = mma_norms(ix, pl);
   // without visited counts or the visited order the search keeps no visited
   // tables, and the array holds only the counter and the ef table
   const bool vis = needs_visited(pl.quant, o);

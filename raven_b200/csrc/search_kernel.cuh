@@ -740,9 +740,10 @@ struct QChunk<1> {  // SQ8: |q-b| per byte, squared by dp4a
 // ---------------------------------------------------------------------------
 // POOLMAX: 64 for pools of at most 64 entries (layout and merge bounds fixed
 // at compile time), 0 for a run-time capacity (a.pool_cap).
-template <int QUANT, int CPL, int POOLMAX, bool VIS>
+template <int QUANT, int CPL, int POOLMAX, bool VIS, bool MMA = false>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : kMinBlocksPerSmPool)
     search_kernel(const SearchArgs a) {
+  static_assert(!MMA || (QUANT == 0 && CPL == 4 && POOLMAX == 0), "tensor-core distances: SQ4, 4 lanes, run-time pool");
   static_assert(VIS || QUANT != 2, "the f32 beam scores new neighbours only: it needs the visited set");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int lane = threadIdx.x & 31;
@@ -867,12 +868,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, VIS ? kMinBlocksPerSm : k
       __syncwarp();  // the query code (and the table) are written before any lane reads them
       QChunk<QUANT> qc;
       qc.load(s.qcode, sub);
-      // SQ4 with four lanes per code and a run-time pool (ef > 64): a row's
-      // distances on the tensor cores as sum q^2 + sum x^2 - 2 sum qx (exact
-      // integers): sum q^2 over all four chunks here, sum x^2 per node from
-      // the upload. (Measured: 5.78 -> 6.11 M QPS at ef=140; with the fixed
-      // 64-entry pool, ef <= 64, the dp4a path stays faster.)
-      constexpr bool kMma = QUANT == 0 && CPL == 4 && POOLMAX == 0;
+      // MMA (SQ4, four lanes per code, run-time pool): a row's distances on
+      // the tensor cores as sum q^2 + sum x^2 - 2 sum qx (exact integers):
+      // sum q^2 over all four chunks here, sum x^2 per node from the upload.
+      // A separate instantiation: the host picks it per launch, and a kernel
+      // holding both paths measured slower on either.
+      constexpr bool kMma = MMA;
       int qqf = 0;
       if constexpr (kMma) {
         qqf = qc.qq + __shfl_xor_sync(kFull, qc.qq, 1);

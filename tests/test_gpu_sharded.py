@@ -158,3 +158,35 @@ def test_gathered_merge_layout_three_ranks(shard_data, oracle):
     with pytest.raises(L.RavenError):  # per_rank must be ceil(n_shards / world)
         L.check(lib.raven_merge_topk_gathered_device(g.data_ptr(), N_SHARDS, world, per + 1, NQ, K, SHARD_SIZE,
                                                      oi_.data_ptr(), od.data_ptr(), oc.data_ptr(), None))
+
+
+@pytest.mark.parametrize("n_shards,k", [(8, 10), (5, 7), (40, 10)])
+def test_merge_kernel_ties_and_short_lists(oracle, n_shards, k):
+    """raven_merge_topk_device against the host merge rule (distance, shard,
+    rank) on lists with many equal distances and shards that return fewer
+    than k results; 8 x 10 and 5 x 7 candidates per query are staged in shared
+    memory, 40 x 10 (above 256) take the unstaged path."""
+    import torch
+    from raven_b200 import _lib as L
+
+    rng = np.random.default_rng(n_shards * 100 + k)
+    nq, size = 300, 1000
+    d = np.sort(rng.integers(0, 12, size=(n_shards, nq, k)).astype(np.float32), axis=2)  # many ties
+    ids = rng.integers(0, size, size=(n_shards, nq, k)).astype(np.uint32)
+    c = rng.integers(0, k + 1, size=(n_shards, nq)).astype(np.uint32)
+    wi, wd, wc = oracle.merge_shard_lists(ids, d, c, size, k)
+
+    def dev(a, dt):
+        return torch.from_numpy(np.ascontiguousarray(a).view(dt)).cuda()
+
+    di, dd, dc = dev(ids, np.int32), dev(d, np.float32), dev(c, np.int32)
+    oi_ = torch.zeros((nq, k), dtype=torch.int32, device="cuda")
+    od = torch.zeros((nq, k), dtype=torch.float32, device="cuda")
+    oc = torch.zeros(nq, dtype=torch.int32, device="cuda")
+    lib = L.load()
+    L.check(lib.raven_merge_topk_device(di.data_ptr(), dd.data_ptr(), dc.data_ptr(), n_shards, nq, k, size,
+                                        oi_.data_ptr(), od.data_ptr(), oc.data_ptr(), None))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(oc.cpu().numpy().view(np.uint32), wc)
+    np.testing.assert_array_equal(oi_.cpu().numpy().view(np.uint32), wi)
+    np.testing.assert_array_equal(od.cpu().numpy(), wd)
