@@ -29,7 +29,7 @@
 // expansion order and every other result are unchanged; a visited neighbour
 // that the pool has dropped is merely scored again (its code was gathered
 // anyway) and rejected. The duplicate test costs one shared read after the
-// binary search that places the candidate: an equal id can only sit in the
+// search that places the candidate: an equal id can only sit in the
 // run of equal distances just before its slot.
 //
 // LinearPool equivalence used by the batch merge: the pool always holds the
